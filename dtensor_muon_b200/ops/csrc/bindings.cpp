@@ -1,0 +1,85 @@
+// Python bindings for the dtensor_muon_b200 sm_100a kernels (module `_C`).
+#include <c10/cuda/CUDAGuard.h>
+#include <cuda_runtime.h>
+#include <torch/extension.h>
+
+#include <mutex>
+
+namespace dmb {
+
+// ---- ortho_gemm.cu
+void gram_sym(const at::Tensor& x, at::Tensor& out, const c10::optional<at::Tensor>& res,
+              const c10::optional<at::Tensor>& scale, double coef_acc, double coef_res, int64_t acc_pow,
+              int64_t res_pow, int64_t max_ctas);
+void gemm_ax(const at::Tensor& a, const at::Tensor& x, at::Tensor& out, const c10::optional<at::Tensor>& res,
+             const c10::optional<at::Tensor>& scale, double coef_acc, double coef_res, int64_t acc_pow,
+             int64_t res_pow, int64_t max_ctas);
+at::Tensor ortho_iterate(at::Tensor x, at::Tensor x2, at::Tensor a_ws, at::Tensor b_ws, const at::Tensor& inv_norm,
+                         const at::Tensor& coeffs, int64_t max_ctas);
+// ---- muon_ops.cu
+at::Tensor muon_pack(const at::Tensor& src_ptrs, const c10::optional<at::Tensor>& buf_ptrs, int64_t src_dtype_code,
+                     int64_t R, int64_t C, int64_t ld, bool transpose, at::Tensor& out, double momentum,
+                     bool nesterov, bool maximize);
+at::Tensor norm_finalize(const at::Tensor& partial, double fac, double eps);
+void muon_apply(const at::Tensor& ws, bool transpose, int64_t R, int64_t C, int64_t ld, const at::Tensor& dst_ptrs,
+                int64_t dst_dtype_code, const c10::optional<at::Tensor>& rowscale, double lr_eff, double wd,
+                bool cautious);
+at::Tensor muon_unpack(const at::Tensor& ws, bool transpose, int64_t R, int64_t C,
+                       const c10::optional<at::Tensor>& mat_scale);
+at::Tensor row_sumsq(const at::Tensor& ws, bool transpose, int64_t R, int64_t C);
+at::Tensor normuon_finalize(const at::Tensor& rowsq, const at::Tensor& v_ptrs, int64_t C, double beta2);
+// ---- adamw.cu
+void adamw_multi(at::Tensor meta_cpu, double lr, double beta1, double beta2, double eps, double wd, bool decoupled,
+                 bool amsgrad, bool maximize, const at::Device& device);
+// ---- lp_quant.cu
+void lp_momentum_step(at::Tensor codes, at::Tensor scale, const at::Tensor& qmap, int64_t fmt, int64_t block,
+                      const at::Tensor& grad, at::Tensor gout, double momentum, bool nesterov, bool maximize);
+at::Tensor lp_dequantize(const at::Tensor& codes, const at::Tensor& scale, const at::Tensor& qmap, int64_t fmt,
+                         int64_t block, int64_t n);
+void lp_quantize(const at::Tensor& x, at::Tensor codes, at::Tensor scale, const at::Tensor& qmap, int64_t fmt,
+                 int64_t block);
+
+// One status word per device. Kernels whose bounded waits give up write an
+// error code here; the host reads and clears it with take_device_error().
+int* device_error_word(int dev) {
+  static int* words[64] = {nullptr};
+  static std::mutex mu;
+  std::lock_guard<std::mutex> lock(mu);
+  if (!words[dev]) {
+    c10::cuda::CUDAGuard g(dev);
+    int* p = nullptr;
+    C10_CUDA_CHECK(cudaMalloc(&p, sizeof(int)));
+    C10_CUDA_CHECK(cudaMemset(p, 0, sizeof(int)));
+    words[dev] = p;
+  }
+  return words[dev];
+}
+
+int64_t take_device_error(int64_t dev) {
+  int* w = device_error_word((int)dev);
+  c10::cuda::CUDAGuard g((int)dev);
+  int v = 0;
+  C10_CUDA_CHECK(cudaMemcpy(&v, w, sizeof(int), cudaMemcpyDeviceToHost));
+  if (v) C10_CUDA_CHECK(cudaMemset(w, 0, sizeof(int)));
+  return v;
+}
+
+}  // namespace dmb
+
+PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
+  m.doc() = "dtensor_muon_b200 sm_100a kernels";
+  m.def("gram_sym", &dmb::gram_sym);
+  m.def("gemm_ax", &dmb::gemm_ax);
+  m.def("ortho_iterate", &dmb::ortho_iterate);
+  m.def("muon_pack", &dmb::muon_pack);
+  m.def("norm_finalize", &dmb::norm_finalize);
+  m.def("muon_apply", &dmb::muon_apply);
+  m.def("muon_unpack", &dmb::muon_unpack);
+  m.def("row_sumsq", &dmb::row_sumsq);
+  m.def("normuon_finalize", &dmb::normuon_finalize);
+  m.def("adamw_multi", &dmb::adamw_multi);
+  m.def("lp_momentum_step", &dmb::lp_momentum_step);
+  m.def("lp_dequantize", &dmb::lp_dequantize);
+  m.def("lp_quantize", &dmb::lp_quantize);
+  m.def("take_device_error", &dmb::take_device_error);
+}

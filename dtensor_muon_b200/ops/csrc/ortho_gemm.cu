@@ -1,0 +1,476 @@
+// Persistent tcgen05 GEMM engine for the Newton-Schulz / Polar Express loop.
+//
+// One kernel, three fused epilogues (reference: the Triton gram_nd kernel and
+// the cuBLAS B@X product of src/muonium/kernels/gram.py:21-106 and
+// src/muonium/orthogonalize/newton_schulz.py:89-103):
+//
+//   GRAM  A   = alpha * X X^T                 symmetric: only tiles touching the
+//                                             upper triangle run; each element is
+//                                             stored exactly once (mirror store)
+//   POLY  B   = c * A A^T + b * A             symmetric, A^T == A
+//   BX    X'  = alpha * (B X) + beta * X      B symmetric, X read MN-major
+//
+// alpha/beta optionally pick up a per-matrix power of `scale[b]`, which is how
+// the Frobenius normalisation of the first iteration is folded into the
+// epilogues instead of a separate pass over X.
+//
+// Layout: every operand is a bf16 [batch, rows, cols] buffer whose rows and
+// cols are multiples of 256 (callers zero-pad), so every tile is full and no
+// store is masked. Tiles are 128 x 256 with a 64-wide K step; operands arrive
+// by TMA (128-byte swizzle, no multicast) into a 4-stage mbarrier ring; one
+// thread issues tcgen05.mma into a double-buffered 2 x 256-column TMEM
+// accumulator; four epilogue warps drain TMEM with tcgen05.ld while the next
+// tile's MMAs run.
+//
+// Warp roles (192 threads): warp 0 TMA producer, warp 1 TMEM owner + MMA
+// issuer, warps 2..5 epilogue (warp w reads TMEM lanes 32*(w%4) .. +31).
+#include <ATen/cuda/CUDAContext.h>
+#include <c10/cuda/CUDAGuard.h>
+#include <torch/extension.h>
+
+#include <mutex>
+
+#include "common.cuh"
+
+namespace dmb {
+
+namespace {
+
+constexpr int BM = 128;
+constexpr int BN = 256;
+constexpr int BK = 64;
+constexpr int STAGES = 4;
+constexpr int A_STAGE = BM * BK * 2;  // 16 KiB
+constexpr int B_STAGE = BN * BK * 2;  // 32 KiB
+constexpr int STAGE_BYTES = A_STAGE + B_STAGE;
+constexpr int THREADS = 192;
+constexpr int TMEM_COLS = 512;
+constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 /*align*/ + 256 /*barriers*/;
+
+struct EpiParams {
+  int batch;
+  int tiles_m, tiles_n, tiles_per_batch, total_tiles;
+  int num_kb;
+  __nv_bfloat16* out;
+  long long out_bstride;
+  int ldo;
+  const __nv_bfloat16* res;
+  long long res_bstride;
+  int ldr;
+  const float* scale;  // per-matrix s, or nullptr (s = 1)
+  float coef_acc, coef_res;
+  int acc_pow, res_pow;  // alpha = coef_acc * s^acc_pow, beta = coef_res * s^res_pow
+  int* err;
+};
+
+__device__ __forceinline__ float ipow(float s, int p) {
+  float r = 1.f;
+  for (int i = 0; i < p; ++i) r *= s;
+  return r;
+}
+
+// Tile order. Symmetric: per matrix, column block tn (256 wide) owns row blocks
+// tm = 0 .. 2*tn+1 (128 high): the tiles that touch the upper triangle.
+template <bool SYM>
+__device__ __forceinline__ void decode_tile(const EpiParams& p, int t, int& b, int& tm, int& tn) {
+  b = t / p.tiles_per_batch;
+  int r = t - b * p.tiles_per_batch;
+  if (SYM) {
+    int c = (int)((sqrtf(4.f * (float)r + 1.f) - 1.f) * 0.5f);
+    while ((c + 1) * (c + 2) <= r) ++c;
+    while (c * (c + 1) > r) --c;
+    tn = c;
+    tm = r - c * (c + 1);
+  } else {
+    tn = r / p.tiles_m;
+    tm = r - tn * p.tiles_m;
+  }
+}
+
+template <bool SYM, bool B_MN>
+__global__ void __launch_bounds__(THREADS, 1)
+    ortho_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                      const EpiParams p) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sA = smem;
+  uint8_t* sB = smem + STAGES * A_STAGE;
+  uint64_t* full = reinterpret_cast<uint64_t*>(sB + STAGES * B_STAGE);
+  uint64_t* empty = full + STAGES;
+  uint64_t* tfull = empty + STAGES;
+  uint64_t* tempty = tfull + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty + 2);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(&tfull[a], 1);
+      mbar_init(&tempty[a], 4);
+    }
+    *abort_flag = 0;
+    fence_mbarrier_init();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&tmA);
+    tma_prefetch_desc(&tmB);
+  }
+  if (warp == 1) tmem_alloc(tmem_slot, TMEM_COLS);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp == 0) {
+    // ------------------------------------------------------- TMA producer --
+    int stage = 0;
+    uint32_t phase = 0;
+    bool ok = true;
+    for (int t = blockIdx.x; ok && t < p.total_tiles; t += gridDim.x) {
+      int b, tm, tn;
+      decode_tile<SYM>(p, t, b, tm, tn);
+      for (int kb = 0; kb < p.num_kb; ++kb) {
+        if (!mbar_wait(&empty[stage], phase ^ 1u, abort_flag, p.err)) {
+          ok = false;
+          break;
+        }
+        if (lane == 0) {
+          mbar_arrive_expect_tx(&full[stage], STAGE_BYTES);
+          tma_load_3d(sA + stage * A_STAGE, &tmA, &full[stage], kb * BK, tm * BM, b);
+          if (!B_MN) {
+            tma_load_3d(sB + stage * B_STAGE, &tmB, &full[stage], kb * BK, tn * BN, b);
+          } else {
+#pragma unroll
+            for (int q = 0; q < BN / 64; ++q)
+              tma_load_3d(sB + stage * B_STAGE + q * (64 * BK * 2), &tmB, &full[stage], tn * BN + q * 64, kb * BK,
+                          b);
+          }
+        }
+        __syncwarp();
+        if (++stage == STAGES) {
+          stage = 0;
+          phase ^= 1u;
+        }
+      }
+    }
+    if (!ok) {
+      // Abort path: give TMA copies already in flight time to land (they
+      // complete in microseconds) before the CTA can exit.
+      const unsigned long long t0 = global_timer_ns();
+      while (global_timer_ns() - t0 < 1000000ull) __nanosleep(1000);
+    }
+  } else if (warp == 1) {
+    // ----------------------------------------------------------- MMA issue --
+    constexpr uint32_t IDESC = idesc_bf16_f32(BM, BN, false, B_MN);
+    const uint32_t a_base = smem_u32(sA);
+    const uint32_t b_base = smem_u32(sB);
+    int stage = 0;
+    uint32_t phase = 0;
+    int acc = 0;
+    uint32_t acc_phase = 0;
+    bool ok = true;
+    for (int t = blockIdx.x; ok && t < p.total_tiles; t += gridDim.x) {
+      if (!mbar_wait(&tempty[acc], acc_phase ^ 1u, abort_flag, p.err)) break;
+      tc_fence_after();
+      const uint32_t d_tmem = tmem_base + (uint32_t)(acc * BN);
+      for (int kb = 0; kb < p.num_kb; ++kb) {
+        if (!mbar_wait(&full[stage], phase, abort_flag, p.err)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        if (lane == 0) {
+#pragma unroll
+          for (int k = 0; k < BK / 16; ++k) {
+            const uint64_t adesc = smem_desc_sw128(a_base + stage * A_STAGE + k * 32, 16, 1024);
+            uint64_t bdesc;
+            if (!B_MN)
+              bdesc = smem_desc_sw128(b_base + stage * B_STAGE + k * 32, 16, 1024);
+            else
+              bdesc = smem_desc_sw128(b_base + stage * B_STAGE + k * 2048, 64 * BK * 2, 1024);
+            tc_mma_bf16(d_tmem, adesc, bdesc, IDESC, (kb | k) != 0 ? 1u : 0u);
+          }
+          tc_commit(&empty[stage]);
+        }
+        __syncwarp();
+        if (++stage == STAGES) {
+          stage = 0;
+          phase ^= 1u;
+        }
+      }
+      if (!ok) break;
+      if (lane == 0) tc_commit(&tfull[acc]);
+      __syncwarp();
+      acc ^= 1;
+      if (acc == 0) acc_phase ^= 1u;
+    }
+  } else {
+    // ------------------------------------------------------------ epilogue --
+    const int q = warp & 3;  // TMEM lane quadrant this warp may access
+    int acc = 0;
+    uint32_t acc_phase = 0;
+    for (int t = blockIdx.x; t < p.total_tiles; t += gridDim.x) {
+      int b, tm, tn;
+      decode_tile<SYM>(p, t, b, tm, tn);
+      if (!mbar_wait(&tfull[acc], acc_phase, abort_flag, p.err)) break;
+      tc_fence_after();
+
+      const float s = p.scale ? p.scale[b] : 1.f;
+      const float alpha = p.coef_acc * ipow(s, p.acc_pow);
+      const float beta = p.coef_res * ipow(s, p.res_pow);
+      const int row = tm * BM + q * 32 + lane;
+      __nv_bfloat16* out_b = p.out + (long long)b * p.out_bstride;
+      const __nv_bfloat16* res_b = p.res ? p.res + (long long)b * p.res_bstride : nullptr;
+
+#pragma unroll 1
+      for (int c = 0; c < BN / 32; ++c) {
+        uint32_t r[32];
+        tmem_ld_32cols(tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc * BN + c * 32), r);
+        const int col0 = tn * BN + c * 32;
+        if (SYM && row > col0 + 31) continue;  // strictly below the diagonal: the mirror covers it
+        float v[32];
+#pragma unroll
+        for (int j = 0; j < 32; ++j) v[j] = alpha * __uint_as_float(r[j]);
+        if (res_b) {
+          const uint4* rp = reinterpret_cast<const uint4*>(res_b + (long long)row * p.ldr + col0);
+#pragma unroll
+          for (int u = 0; u < 4; ++u) {
+            uint4 x = __ldg(rp + u);
+            const uint32_t w[4] = {x.x, x.y, x.z, x.w};
+#pragma unroll
+            for (int h = 0; h < 4; ++h) {
+              v[u * 8 + h * 2 + 0] += beta * bf16_bits_to_float((uint16_t)(w[h] & 0xFFFFu));
+              v[u * 8 + h * 2 + 1] += beta * bf16_bits_to_float((uint16_t)(w[h] >> 16));
+            }
+          }
+        }
+        if (!SYM || row <= col0) {
+          // Whole 32-column chunk is on or above the diagonal (or not symmetric).
+          uint4* op = reinterpret_cast<uint4*>(out_b + (long long)row * p.ldo + col0);
+#pragma unroll
+          for (int u = 0; u < 4; ++u) {
+            uint4 x;
+            x.x = pack_bf16x2(v[u * 8 + 0], v[u * 8 + 1]);
+            x.y = pack_bf16x2(v[u * 8 + 2], v[u * 8 + 3]);
+            x.z = pack_bf16x2(v[u * 8 + 4], v[u * 8 + 5]);
+            x.w = pack_bf16x2(v[u * 8 + 6], v[u * 8 + 7]);
+            op[u] = x;
+          }
+          if (SYM) {
+#pragma unroll
+            for (int j = 0; j < 32; ++j)
+              if (row < col0 + j) out_b[(long long)(col0 + j) * p.ldo + row] = __float2bfloat16_rn(v[j]);
+          }
+        } else {
+          // Chunk straddles the diagonal: per-element ownership.
+#pragma unroll
+          for (int j = 0; j < 32; ++j) {
+            const int col = col0 + j;
+            if (row <= col) {
+              const __nv_bfloat16 hv = __float2bfloat16_rn(v[j]);
+              out_b[(long long)row * p.ldo + col] = hv;
+              if (row < col) out_b[(long long)col * p.ldo + row] = hv;
+            }
+          }
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&tempty[acc]);
+      acc ^= 1;
+      if (acc == 0) acc_phase ^= 1u;
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, TMEM_COLS);
+  }
+}
+
+// ------------------------------------------------------------------ host --
+using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                   const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                   CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn get_encode_fn() {
+  static EncodeTiledFn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* ptr = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    cudaError_t e = cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q);
+    TORCH_CHECK(e == cudaSuccess && q == cudaDriverEntryPointSuccess && ptr,
+                "dtensor_muon_b200: cannot resolve cuTensorMapEncodeTiled");
+    fn = reinterpret_cast<EncodeTiledFn>(ptr);
+  });
+  return fn;
+}
+
+// bf16 [batch, rows, cols] tensor map with a (64 x box_rows x 1) box, 128-byte swizzle.
+CUtensorMap make_map(const at::Tensor& t, int box_cols, int box_rows) {
+  TORCH_CHECK(t.dim() == 3 && t.scalar_type() == at::kBFloat16 && t.is_cuda());
+  TORCH_CHECK(t.stride(2) == 1, "innermost dim must be contiguous");
+  CUtensorMap map;
+  cuuint64_t dims[3] = {(cuuint64_t)t.size(2), (cuuint64_t)t.size(1), (cuuint64_t)t.size(0)};
+  cuuint64_t strides[2] = {(cuuint64_t)t.stride(1) * 2, (cuuint64_t)t.stride(0) * 2};
+  cuuint32_t box[3] = {(cuuint32_t)box_cols, (cuuint32_t)box_rows, 1};
+  cuuint32_t estr[3] = {1, 1, 1};
+  CUresult r = get_encode_fn()(&map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, t.data_ptr(), dims, strides, box, estr,
+                               CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                               CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  TORCH_CHECK(r == CUDA_SUCCESS, "cuTensorMapEncodeTiled failed: ", (int)r);
+  return map;
+}
+
+int num_sms(int dev) {
+  static int cache[64] = {0};
+  if (!cache[dev]) {
+    int v = 0;
+    cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, dev);
+    cache[dev] = v;
+  }
+  return cache[dev];
+}
+
+template <bool SYM, bool B_MN>
+void launch(const CUtensorMap& ma, const CUtensorMap& mb, const EpiParams& p, int max_ctas, cudaStream_t st) {
+  static bool configured[64] = {false};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (!configured[dev]) {
+    C10_CUDA_CHECK(cudaFuncSetAttribute(ortho_gemm_kernel<SYM, B_MN>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                        SMEM_BYTES));
+    configured[dev] = true;
+  }
+  int grid = std::min(p.total_tiles, max_ctas > 0 ? max_ctas : num_sms(dev));
+  if (grid <= 0) return;
+  ortho_gemm_kernel<SYM, B_MN><<<grid, THREADS, SMEM_BYTES, st>>>(ma, mb, p);
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+void check_ws(const at::Tensor& t, const char* name) {
+  TORCH_CHECK(t.is_cuda() && t.dim() == 3 && t.scalar_type() == at::kBFloat16, name, ": bf16 [B,R,C] CUDA");
+  TORCH_CHECK(t.is_contiguous(), name, " must be contiguous");
+  TORCH_CHECK(t.size(1) % 256 == 0 && t.size(2) % 256 == 0, name, ": rows/cols must be multiples of 256");
+}
+
+}  // namespace
+
+int* device_error_word(int dev);
+
+// out[b] = coef_acc * s_b^acc_pow * x[b] x[b]^T  (+ coef_res * s_b^res_pow * res[b])
+// x: [B, N, K]; out, res: [B, N, N]. Symmetric store.
+void gram_sym(const at::Tensor& x, at::Tensor& out, const c10::optional<at::Tensor>& res,
+              const c10::optional<at::Tensor>& scale, double coef_acc, double coef_res, int64_t acc_pow,
+              int64_t res_pow, int64_t max_ctas) {
+  check_ws(x, "x");
+  check_ws(out, "out");
+  const int B = x.size(0), N = x.size(1), K = x.size(2);
+  TORCH_CHECK(out.size(0) == B && out.size(1) == N && out.size(2) == N, "out must be [B,N,N]");
+  const at::cuda::CUDAGuard guard(x.device());
+  EpiParams p{};
+  p.batch = B;
+  p.tiles_m = N / BM;
+  p.tiles_n = N / BN;
+  p.tiles_per_batch = p.tiles_n * (p.tiles_n + 1);
+  p.total_tiles = B * p.tiles_per_batch;
+  p.num_kb = K / BK;
+  p.out = reinterpret_cast<__nv_bfloat16*>(out.data_ptr());
+  p.out_bstride = out.stride(0);
+  p.ldo = out.stride(1);
+  if (res.has_value()) {
+    check_ws(*res, "res");
+    TORCH_CHECK(res->sizes() == out.sizes());
+    p.res = reinterpret_cast<const __nv_bfloat16*>(res->data_ptr());
+    p.res_bstride = res->stride(0);
+    p.ldr = res->stride(1);
+  }
+  if (scale.has_value()) {
+    TORCH_CHECK(scale->scalar_type() == at::kFloat && scale->numel() >= B && scale->is_cuda());
+    p.scale = scale->data_ptr<float>();
+  }
+  p.coef_acc = (float)coef_acc;
+  p.coef_res = (float)coef_res;
+  p.acc_pow = (int)acc_pow;
+  p.res_pow = (int)res_pow;
+  p.err = device_error_word(x.get_device());
+  CUtensorMap ma = make_map(x, BK, BM);
+  CUtensorMap mb = make_map(x, BK, BN);
+  launch<true, false>(ma, mb, p, (int)max_ctas, at::cuda::getCurrentCUDAStream());
+}
+
+// out[b] = coef_acc * s^acc_pow * (a[b] @ x[b]) + coef_res * s^res_pow * res[b]
+// a: [B, N, N] (used as A K-major: rows of a), x: [B, N, M] (MN-major B), out/res: [B, N, M].
+void gemm_ax(const at::Tensor& a, const at::Tensor& x, at::Tensor& out, const c10::optional<at::Tensor>& res,
+             const c10::optional<at::Tensor>& scale, double coef_acc, double coef_res, int64_t acc_pow,
+             int64_t res_pow, int64_t max_ctas) {
+  check_ws(a, "a");
+  check_ws(x, "x");
+  check_ws(out, "out");
+  const int B = x.size(0), N = x.size(1), M = x.size(2);
+  TORCH_CHECK(a.size(0) == B && a.size(1) == N && a.size(2) == N, "a must be [B,N,N]");
+  TORCH_CHECK(out.sizes() == x.sizes(), "out must match x");
+  const at::cuda::CUDAGuard guard(x.device());
+  EpiParams p{};
+  p.batch = B;
+  p.tiles_m = N / BM;
+  p.tiles_n = M / BN;
+  p.tiles_per_batch = p.tiles_m * p.tiles_n;
+  p.total_tiles = B * p.tiles_per_batch;
+  p.num_kb = N / BK;
+  p.out = reinterpret_cast<__nv_bfloat16*>(out.data_ptr());
+  p.out_bstride = out.stride(0);
+  p.ldo = out.stride(1);
+  if (res.has_value()) {
+    check_ws(*res, "res");
+    TORCH_CHECK(res->sizes() == out.sizes());
+    p.res = reinterpret_cast<const __nv_bfloat16*>(res->data_ptr());
+    p.res_bstride = res->stride(0);
+    p.ldr = res->stride(1);
+  }
+  if (scale.has_value()) {
+    TORCH_CHECK(scale->scalar_type() == at::kFloat && scale->numel() >= B && scale->is_cuda());
+    p.scale = scale->data_ptr<float>();
+  }
+  p.coef_acc = (float)coef_acc;
+  p.coef_res = (float)coef_res;
+  p.acc_pow = (int)acc_pow;
+  p.res_pow = (int)res_pow;
+  p.err = device_error_word(x.get_device());
+  CUtensorMap ma = make_map(a, BK, BM);
+  CUtensorMap mb = make_map(x, 64, BK);
+  launch<false, true>(ma, mb, p, (int)max_ctas, at::cuda::getCurrentCUDAStream());
+}
+
+// Full iteration on a zero-padded workspace. x holds the (unnormalised) bf16
+// matrices [B, N, M] with N <= M; inv_norm[b] = 1 / (||X_b|| * fac + eps).
+// coeffs: [steps, 3] (a, b, c) on the host. Returns the buffer holding the result
+// (x or x2). a_ws, b_ws: [B, N, N] scratch.
+at::Tensor ortho_iterate(at::Tensor x, at::Tensor x2, at::Tensor a_ws, at::Tensor b_ws, const at::Tensor& inv_norm,
+                         const at::Tensor& coeffs, int64_t max_ctas) {
+  TORCH_CHECK(coeffs.device().is_cpu() && coeffs.scalar_type() == at::kDouble && coeffs.dim() == 2 &&
+              coeffs.size(1) == 3);
+  const int steps = coeffs.size(0);
+  auto c = coeffs.accessor<double, 2>();
+  at::Tensor cur = x, nxt = x2;
+  for (int s = 0; s < steps; ++s) {
+    const bool first = (s == 0);
+    c10::optional<at::Tensor> sc = first ? c10::optional<at::Tensor>(inv_norm) : c10::nullopt;
+    gram_sym(cur, a_ws, c10::nullopt, sc, 1.0, 0.0, first ? 2 : 0, 0, max_ctas);
+    gram_sym(a_ws, b_ws, a_ws, c10::nullopt, c[s][2], c[s][1], 0, 0, max_ctas);
+    gemm_ax(b_ws, cur, nxt, cur, sc, 1.0, c[s][0], first ? 1 : 0, first ? 1 : 0, max_ctas);
+    std::swap(cur, nxt);
+  }
+  return cur;
+}
+
+}  // namespace dmb

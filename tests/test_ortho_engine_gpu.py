@@ -1,0 +1,72 @@
+"""Numerics of the tcgen05 orthogonalisation engine against fp32 PyTorch."""
+
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+from dtensor_muon_b200.ops import _ext, ortho
+from dtensor_muon_b200.orthogonalize.newton_schulz import ns_loop
+from dtensor_muon_b200.orthogonalize.polar_express import pe_loop
+
+
+def _close_frac(a, b, rtol, atol):
+    return (~torch.isclose(a.float(), b.float(), rtol=rtol, atol=atol)).float().mean().item()
+
+
+@pytest.mark.parametrize("shape", [(1, 256, 256), (2, 300, 520), (3, 512, 1024), (1, 1024, 4096), (2, 96, 40)])
+def test_gram_matches_fp32(shape):
+    torch.manual_seed(0)
+    x = torch.randn(*shape, device="cuda").bfloat16()
+    y = ortho.gram(x)
+    ref = x.float() @ x.float().mT
+    torch.testing.assert_close(y.float(), ref, rtol=2e-2, atol=2e-2 * shape[-1] ** 0.5)
+    assert torch.equal(y, y.mT), "gram output must be exactly symmetric"
+    _ext.check_device_errors("cuda")
+
+
+@pytest.mark.parametrize("B,N,M", [(1, 256, 256), (2, 256, 768), (3, 512, 1024)])
+def test_gemm_ax_matches_fp32(B, N, M):
+    torch.manual_seed(1)
+    C = _ext.load()
+    a = torch.randn(B, N, N, device="cuda").bfloat16()
+    x = torch.randn(B, N, M, device="cuda").bfloat16()
+    res = torch.randn(B, N, M, device="cuda").bfloat16()
+    out = torch.empty_like(x)
+    C.gemm_ax(a, x, out, res, None, 0.5, -1.5, 0, 0, 0)
+    ref = 0.5 * (a.float() @ x.float()) - 1.5 * res.float()
+    torch.testing.assert_close(out.float(), ref, rtol=2e-2, atol=3e-2 * N**0.5)
+    _ext.check_device_errors("cuda")
+
+
+def test_gram_poly_epilogue():
+    torch.manual_seed(2)
+    C = _ext.load()
+    x = torch.randn(2, 512, 512, device="cuda")
+    a = (x @ x.mT / 512).bfloat16()  # symmetric
+    out = torch.empty_like(a)
+    C.gram_sym(a, out, a, None, 2.0, -3.0, 0, 0, 0)
+    ref = 2.0 * (a.float() @ a.float()) - 3.0 * a.float()
+    torch.testing.assert_close(out.float(), ref, rtol=2e-2, atol=5e-2)
+
+
+@pytest.mark.parametrize("strategy", ["newton_schulz", "polar_express"])
+@pytest.mark.parametrize("shape", [(4, 256, 256), (2, 384, 200), (2, 200, 384), (1, 1024, 3072), (3, 17, 33)])
+def test_orthogonalize_matches_torch(strategy, shape):
+    torch.manual_seed(3)
+    g = torch.randn(*shape, device="cuda")
+    got = torch.stack(ortho.orthogonalize_native(list(g.unbind(0)), 5, strategy, 1e-7))
+    loop = ns_loop if strategy == "newton_schulz" else pe_loop
+    ref = loop(g.double(), 5, eps=1e-7).float()
+    assert got.dtype == torch.bfloat16 and got.shape == g.shape
+    # bf16 iteration vs fp64: the reference's own triton-vs-eager budget.
+    frac = _close_frac(got, ref, rtol=1e-2, atol=5e-2)
+    assert frac < 0.02, frac
+    _ext.check_device_errors("cuda")
+
+
+def test_orthogonalize_steps0_is_normalized_input():
+    g = torch.randn(2, 64, 128, device="cuda")
+    got = torch.stack(ortho.orthogonalize_native(list(g.unbind(0)), 0, "newton_schulz", 1e-7))
+    ref = g / (g.norm(dim=(-2, -1), keepdim=True) + 1e-7)
+    torch.testing.assert_close(got.float(), ref, rtol=1e-2, atol=1e-3)
