@@ -12,6 +12,45 @@ import importlib
 _C = None
 _IMPORT_ERROR: Exception | None = None
 
+# Kernel launches issued by each binding (ortho_iterate: three per step).
+_LAUNCHES = {
+    "gram_sym": 1,
+    "gemm_ax": 1,
+    "muon_pack": 1,
+    "norm_finalize": 1,
+    "muon_apply": 1,
+    "muon_unpack": 1,
+    "row_sumsq": 1,
+    "normuon_finalize": 1,
+    "adamw_multi": 1,
+    "lp_momentum_step": 1,
+    "lp_dequantize": 1,
+    "lp_quantize": 1,
+}
+launch_count = 0
+
+
+class _Counted:
+    """Thin proxy over the extension that counts the kernels each call launches."""
+
+    def __init__(self, mod):
+        self._mod = mod
+
+    def __getattr__(self, name):
+        fn = getattr(self._mod, name)
+        if not callable(fn):
+            return fn
+
+        def call(*args, **kwargs):
+            global launch_count
+            if name == "ortho_iterate":
+                launch_count += 3 * int(args[5].shape[0])
+            else:
+                launch_count += _LAUNCHES.get(name, 0)
+            return fn(*args, **kwargs)
+
+        return call
+
 
 def load():
     """Return the compiled extension module, importing it on first use."""
@@ -24,7 +63,7 @@ def load():
             "(run `python setup.py build_ext --inplace`)"
         ) from _IMPORT_ERROR
     try:
-        _C = importlib.import_module("dtensor_muon_b200._C")
+        _C = _Counted(importlib.import_module("dtensor_muon_b200._C"))
     except Exception as exc:  # pragma: no cover - depends on the build
         _IMPORT_ERROR = exc
         raise RuntimeError(

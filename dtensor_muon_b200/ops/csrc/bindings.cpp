@@ -22,8 +22,8 @@ at::Tensor muon_pack(const at::Tensor& src_ptrs, const c10::optional<at::Tensor>
                      bool nesterov, bool maximize);
 at::Tensor norm_finalize(const at::Tensor& partial, double fac, double eps);
 void muon_apply(const at::Tensor& ws, bool transpose, int64_t R, int64_t C, int64_t ld, const at::Tensor& dst_ptrs,
-                int64_t dst_dtype_code, const c10::optional<at::Tensor>& rowscale, double lr_eff, double wd,
-                bool cautious);
+                int64_t dst_dtype_code, const c10::optional<at::Tensor>& rowscale,
+                const c10::optional<at::Tensor>& mat_scale, double lr_eff, double wd, bool cautious);
 at::Tensor muon_unpack(const at::Tensor& ws, bool transpose, int64_t R, int64_t C,
                        const c10::optional<at::Tensor>& mat_scale);
 at::Tensor row_sumsq(const at::Tensor& ws, bool transpose, int64_t R, int64_t C);

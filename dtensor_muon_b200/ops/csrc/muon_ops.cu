@@ -262,13 +262,6 @@ __global__ void __launch_bounds__(256) normuon_finalize_kernel(const float* rows
   for (int r = threadIdx.x; r < R; r += 256) rowscale[(long long)b * R + r] *= fac;
 }
 
-int dtype_code(at::ScalarType t) {
-  if (t == at::kFloat) return 0;
-  if (t == at::kBFloat16) return 1;
-  TORCH_CHECK(false, "dtensor_muon_b200: unsupported dtype ", t, " (fp32 / bf16 only)");
-  return -1;
-}
-
 }  // namespace
 
 // Packs B matrices (pointers in `src`, optional fp32 momentum `buf`) into the
@@ -319,8 +312,8 @@ at::Tensor norm_finalize(const at::Tensor& partial, double fac, double eps) {
 }
 
 void muon_apply(const at::Tensor& ws, bool transpose, int64_t R, int64_t C, int64_t ld, const at::Tensor& dst_ptrs,
-                int64_t dst_dtype_code, const c10::optional<at::Tensor>& rowscale, double lr_eff, double wd,
-                bool cautious) {
+                int64_t dst_dtype_code, const c10::optional<at::Tensor>& rowscale,
+                const c10::optional<at::Tensor>& mat_scale, double lr_eff, double wd, bool cautious) {
   const at::cuda::CUDAGuard guard(ws.device());
   const int B = ws.size(0);
   ApplyArgs a{};
@@ -334,6 +327,7 @@ void muon_apply(const at::Tensor& ws, bool transpose, int64_t R, int64_t C, int6
   a.dst = dst_ptrs.data_ptr<int64_t>();
   a.dst_dtype = (int)dst_dtype_code;
   a.rowscale = rowscale.has_value() ? rowscale->data_ptr<float>() : nullptr;
+  a.mat_scale = mat_scale.has_value() ? mat_scale->data_ptr<float>() : nullptr;
   a.lr_eff = (float)lr_eff;
   a.wd = (float)wd;
   a.cautious = cautious;

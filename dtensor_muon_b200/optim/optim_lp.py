@@ -1,0 +1,357 @@
+"""``MuonLP``: Muon with block-quantised momentum state.
+
+API of the reference's ``muonium.optim.optim_lp`` (src/muonium/optim/optim_lp.py:21-133):
+``MuonLP(..., foreach=False, block_size=2048, bf16_stochastic_round=False)``
+plus ``Muon8bit`` / ``Muon4bit`` / ``MuonFp8``. Only ``like="grad"`` buffers
+(the momentum) are quantised, and only when the local tensor has at least 4096
+elements and a multiple of ``block_size``; row-shaped buffers stay fp32. The
+base ``MuonLP`` stores plain fp32 buffers.
+
+The reference builds these buffers from torchao subclasses but cannot step
+them. Here the state is a :class:`QuantizedState` (codes + one fp32 scale per
+block + the code map) and a step is: dequantise, momentum update in fp32,
+requantise per block. On CUDA with a built-in algorithm that is one fused
+kernel per tensor (``lp_momentum_step``) feeding the orthogonalisation
+workspace; every other case dequantises into an fp32 temporary, runs the
+algorithm's normal update and requantises.
+"""
+
+from __future__ import annotations
+
+import torch
+from torch import Tensor
+from torch.distributed.tensor import DTensor
+
+from ..ops import _ext, muon_fused
+from ..orthogonalize import OrthogonalizationStrategy
+from ..utils import to_local
+from .algorithms import BufferSpec, MuonAlgorithm
+from .algorithms import base as algo_base
+from .algorithms.muon import MuonBaseline, lr_effs
+from .algorithms.normuon import NorMuon
+from .optim import Muon
+
+FMT_FP8, FMT_8BIT, FMT_4BIT = 0, 1, 2
+_FMT_BITS = {FMT_8BIT: 8, FMT_4BIT: 4}
+
+
+def dynamic_tree_map(total_bits: int, signed: bool = True) -> Tensor:
+    """Sorted code map of dynamic tree quantisation (Dettmers, arXiv:1511.04561).
+
+    After an optional sign bit, ``k`` leading zero bits select the decade
+    ``10**-k`` and the bits after the first one-bit split ``(0.1, 1]`` of that
+    decade into equal steps (right edges, so 1.0 itself is a code). Zero is a
+    code; a signed map is padded with a second zero to ``2**total_bits`` entries.
+    """
+    value_bits = total_bits - (1 if signed else 0)
+    mags: list[float] = []
+    for k in range(value_bits):
+        n = 2 ** (value_bits - k - 1)
+        mags += [(0.1 + 0.9 * (i + 1) / n) * 10.0 ** (-k) for i in range(n)]
+    vals = [0.0] + mags + ([-m for m in mags] if signed else [])
+    while len(vals) < 2**total_bits:
+        vals.append(0.0)
+    return torch.tensor(sorted(vals), dtype=torch.float32)
+
+
+_QMAPS: dict[tuple, Tensor] = {}
+
+
+def qmap_for(fmt: int, signed: bool, device: torch.device) -> Tensor:
+    if fmt == FMT_FP8:
+        key = (fmt, True, str(device))
+        if key not in _QMAPS:
+            _QMAPS[key] = torch.zeros(1, dtype=torch.float32, device=device)
+        return _QMAPS[key]
+    key = (fmt, signed, str(device))
+    if key not in _QMAPS:
+        _QMAPS[key] = dynamic_tree_map(_FMT_BITS[fmt], signed).to(device)
+    return _QMAPS[key]
+
+
+def _nearest_codes(x: Tensor, qmap: Tensor) -> Tensor:
+    """Index of the nearest map entry (ties to the lower index), CPU path."""
+    hi = torch.searchsorted(qmap, x.contiguous(), right=True).clamp(1, qmap.numel() - 1)
+    lo = hi - 1
+    pick_hi = (qmap[hi] - x).abs() < (x - qmap[lo]).abs()
+    return torch.where(pick_hi, hi, lo).to(torch.uint8)
+
+
+class QuantizedState:
+    """Block-quantised fp32 tensor: ``codes`` (uint8), ``scale`` (fp32, one per
+    block), the code map ``qmap``, ``fmt`` (0 fp8 e4m3, 1 8-bit map, 2 4-bit
+    map), ``block_size``, ``signed`` and the logical ``shape``."""
+
+    def __init__(self, codes: Tensor, scale: Tensor, qmap: Tensor, fmt: int, block_size: int, signed: bool, shape):
+        self.codes = codes
+        self.scale = scale
+        self.qmap = qmap
+        self.fmt = int(fmt)
+        self.block_size = int(block_size)
+        self.signed = bool(signed)
+        self.shape = torch.Size(shape)
+
+    # -- construction ------------------------------------------------------
+    @classmethod
+    def zeros(cls, shape, fmt: int, block_size: int, signed: bool, device) -> "QuantizedState":
+        n = 1
+        for s in shape:
+            n *= int(s)
+        nbytes = (n + 1) // 2 if fmt == FMT_4BIT else n
+        qmap = qmap_for(fmt, signed, torch.device(device))
+        zero_code = 0
+        if fmt != FMT_FP8:
+            zero_code = int(torch.nonzero(qmap.cpu() == 0)[0])
+        codes = torch.full((nbytes,), zero_code | (zero_code << 4) if fmt == FMT_4BIT else zero_code,
+                           dtype=torch.uint8, device=device)
+        scale = torch.zeros((n + block_size - 1) // block_size, dtype=torch.float32, device=device)
+        return cls(codes, scale, qmap, fmt, block_size, signed, shape)
+
+    # -- tensor-like surface -----------------------------------------------
+    @property
+    def device(self) -> torch.device:
+        return self.codes.device
+
+    @property
+    def dtype(self) -> torch.dtype:
+        return torch.float32
+
+    def numel(self) -> int:
+        n = 1
+        for s in self.shape:
+            n *= s
+        return n
+
+    def dim(self) -> int:
+        return len(self.shape)
+
+    ndim = property(dim)
+
+    def size(self, d=None):
+        return self.shape if d is None else self.shape[d]
+
+    def dequantize(self) -> Tensor:
+        n = self.numel()
+        if self.codes.is_cuda:
+            out = _ext.load().lp_dequantize(self.codes, self.scale, self.qmap, self.fmt, self.block_size, n)
+            return out.view(self.shape)
+        scale = self.scale.repeat_interleave(self.block_size)[:n]
+        if self.fmt == FMT_FP8:
+            vals = self.codes.view(torch.float8_e4m3fn).float()
+        elif self.fmt == FMT_8BIT:
+            vals = self.qmap[self.codes.long()]
+        else:
+            lo = (self.codes & 15).long()
+            hi = (self.codes >> 4).long()
+            vals = self.qmap[torch.stack([lo, hi], dim=1).reshape(-1)[:n]]
+        return (vals * scale).view(self.shape)
+
+    def copy_(self, src: Tensor) -> "QuantizedState":
+        """Requantise from an fp32 tensor with this state's shape."""
+        x = src.detach().to(self.device, torch.float32).contiguous().view(-1)
+        if self.codes.is_cuda:
+            _ext.load().lp_quantize(x, self.codes, self.scale, self.qmap, self.fmt, self.block_size)
+            return self
+        n = x.numel()
+        nb = self.scale.numel()
+        padded = torch.zeros(nb * self.block_size, dtype=torch.float32)
+        padded[:n] = x
+        blocks = padded.view(nb, self.block_size)
+        amax = blocks.abs().amax(dim=1)
+        s = amax / 448.0 if self.fmt == FMT_FP8 else amax
+        inv = torch.where(s > 0, 1.0 / s, torch.zeros_like(s))
+        y = (blocks * inv[:, None]).view(-1)[:n]
+        self.scale.copy_(s)
+        if self.fmt == FMT_FP8:
+            self.codes.copy_(y.to(torch.float8_e4m3fn).view(torch.uint8))
+        else:
+            codes = _nearest_codes(y, self.qmap)
+            if self.fmt == FMT_4BIT:
+                if n % 2:
+                    codes = torch.cat([codes, codes.new_zeros(1)])
+                pairs = codes.view(-1, 2)
+                codes = pairs[:, 0] | (pairs[:, 1] << 4)
+            self.codes.copy_(codes)
+        return self
+
+    def to(self, device) -> "QuantizedState":
+        return QuantizedState(
+            self.codes.to(device), self.scale.to(device), self.qmap.to(device), self.fmt, self.block_size,
+            self.signed, self.shape,
+        )
+
+    def __repr__(self) -> str:
+        return f"QuantizedState(shape={tuple(self.shape)}, fmt={self.fmt}, block_size={self.block_size})"
+
+
+try:  # allow torch.load(weights_only=True) of MuonLP checkpoints
+    torch.serialization.add_safe_globals([QuantizedState, torch.Size])
+except AttributeError:  # pragma: no cover
+    pass
+
+
+class MuonLP(Muon):
+    """Low-precision Muon: momentum buffers stored block-quantised."""
+
+    #: quantisation format of the subclass; None keeps fp32 buffers
+    _fmt: int | None = None
+
+    def __init__(
+        self,
+        params,
+        lr: float = 1e-3,
+        wd: float = 0.1,
+        use_cautious_wd: bool = True,
+        maximize: bool = False,
+        momentum: float = 0.95,
+        nesterov: bool = True,
+        ns_steps: int = 5,
+        orthogonalization_strategy: OrthogonalizationStrategy = "polar_express",
+        amsgrad: bool = False,
+        adam_betas: tuple[float, float] = (0.9, 0.95),
+        adam_eps: float = 1e-8,
+        is_adamw: bool = True,
+        foreach_adam: bool | None = None,
+        fused_adam: bool | None = None,
+        foreach: bool | None = False,
+        batch_size: int | None = None,
+        block_size: int = 2048,
+        bf16_stochastic_round: bool = False,
+    ):
+        super().__init__(
+            params=params,
+            lr=lr,
+            wd=wd,
+            use_cautious_wd=use_cautious_wd,
+            maximize=maximize,
+            momentum=momentum,
+            nesterov=nesterov,
+            ns_steps=ns_steps,
+            orthogonalization_strategy=orthogonalization_strategy,
+            amsgrad=amsgrad,
+            adam_betas=adam_betas,
+            adam_eps=adam_eps,
+            is_adamw=is_adamw,
+            fused_adam=fused_adam,
+            foreach_adam=foreach_adam,
+            foreach=foreach,
+            batch_size=batch_size,
+        )
+        self.block_size = block_size
+        # Kept for API compatibility; the updates write fp32/bf16 params with
+        # round-to-nearest.
+        self.bf16_stochastic_round = bf16_stochastic_round
+
+    @classmethod
+    def _subclass_zeros(cls, p: Tensor, signed: bool, block_size: int):
+        """Quantised zeros for ``p``'s shape, or plain fp32 zeros in the base class."""
+        if cls._fmt is None:
+            return torch.zeros_like(p, dtype=torch.float32)
+        return QuantizedState.zeros(p.shape, cls._fmt, block_size, signed, p.device)
+
+    def _new_buffer(self, p: Tensor, signed: bool):
+        local = to_local(p)
+        if local.numel() >= 4096 and local.numel() % self.block_size == 0:
+            return self._subclass_zeros(local, signed, self.block_size)
+        return torch.zeros_like(local, dtype=torch.float32)
+
+    def _new_state_buffer(self, p: Tensor, grad: Tensor, spec: BufferSpec):
+        if spec.like == "grad":
+            buf = self._new_buffer(grad, spec.signed)
+            if isinstance(buf, Tensor) and isinstance(grad, DTensor):
+                return DTensor.from_local(
+                    buf, device_mesh=grad.device_mesh, placements=grad.placements, run_check=False,
+                    shape=grad.shape, stride=grad.stride(),
+                )
+            return buf
+        return super()._new_state_buffer(p, grad, spec)
+
+    # ---------------------------------------------------------------- driver
+    def muon(self, algorithm: MuonAlgorithm, params, grads, state, lr_ratios, **kw):
+        if not params:
+            return
+        quant_keys = [k for k, v in state.items() if any(isinstance(b, QuantizedState) for b in v)]
+        if not quant_keys:
+            return super().muon(algorithm, params, grads, state, lr_ratios, **kw)
+        opts = {k: v for k, v in kw.items() if k not in ("foreach",)}
+        for i, (p, g, r) in enumerate(zip(params, grads, lr_ratios, strict=True)):
+            st = {k: v[i] for k, v in state.items()}
+            if self._fused_lp(algorithm, p, g, st, r, opts):
+                continue
+            # Generic: dequantise into fp32 temporaries, normal update, requantise.
+            temps = {}
+            for k in quant_keys:
+                q = st[k]
+                if isinstance(q, QuantizedState):
+                    t = q.dequantize()
+                    if isinstance(g, DTensor):
+                        t = DTensor.from_local(
+                            t, device_mesh=g.device_mesh, placements=g.placements, run_check=False,
+                            shape=g.shape, stride=g.stride(),
+                        )
+                    temps[k] = (q, t)
+                    st[k] = t
+            super().muon(
+                algorithm, [p], [g], {k: [v] for k, v in st.items()}, [r], foreach=False, **opts
+            )
+            for k, (q, t) in temps.items():
+                q.copy_(to_local(t))
+
+    def _fused_lp(self, algorithm, p, g, st, lr_ratio, opts) -> bool:
+        q = st.get("momentum_buffer")
+        if not isinstance(q, QuantizedState) or not q.codes.is_cuda:
+            return False
+        if type(algorithm) not in (MuonBaseline, NorMuon) or not algo_base._seams_are_builtin():
+            return False
+        if opts.get("split_sizes") is not None or isinstance(p, DTensor) or isinstance(g, DTensor):
+            return False
+        if not (p.is_contiguous() and g.is_contiguous() and _ext.available()):
+            return False
+        if p.dtype not in (torch.float32, torch.bfloat16) or g.dtype not in (torch.float32, torch.bfloat16):
+            return False
+        variances = None
+        if isinstance(algorithm, NorMuon):
+            v = st["variance_neuron"]
+            if isinstance(v, QuantizedState) or not (v.is_cuda and v.is_contiguous()):
+                return False
+            variances = [v]
+        g_eff = torch.empty(g.shape, dtype=torch.bfloat16, device=g.device)
+        _ext.load().lp_momentum_step(
+            q.codes, q.scale, q.qmap, q.fmt, q.block_size, g, g_eff, float(opts["momentum"]),
+            bool(opts["nesterov"]), bool(opts["maximize"]),
+        )
+        muon_fused.fused_muon_update(
+            [p],
+            [g_eff],
+            [g_eff],
+            lr_effs(opts["lr"], [lr_ratio]),
+            weight_decay=opts["weight_decay"],
+            cautious_wd=opts["cautious_wd"],
+            momentum=0.0,
+            nesterov=False,
+            maximize=False,
+            ns_steps=opts["ns_steps"],
+            strategy=opts["orthogonalization_strategy"],
+            variances=variances,
+            muon_beta2=opts.get("muon_beta2", 0.95),
+            momentum_done=True,
+        )
+        return True
+
+
+class Muon8bit(MuonLP):
+    """MuonLP with 8-bit dynamic-tree momentum."""
+
+    _fmt = FMT_8BIT
+
+
+class Muon4bit(MuonLP):
+    """MuonLP with 4-bit dynamic-tree momentum (two codes per byte)."""
+
+    _fmt = FMT_4BIT
+
+
+class MuonFp8(MuonLP):
+    """MuonLP with fp8 (e4m3) block-scaled momentum."""
+
+    _fmt = FMT_FP8

@@ -1,0 +1,88 @@
+"""Training harness: model construction (optionally FSDP2-sharded), the Muon +
+AdamW optimizer split, synthetic data and one training step.
+
+This is the public entry point a user calls to train with the framework:
+
+    model = build_llama(preset("llama3-8b"), device)
+    opt = build_optimizer(model)
+    trainer = Trainer(model, opt)
+    loss = trainer.step(tokens, targets)
+"""
+
+from __future__ import annotations
+
+import torch
+import torch.distributed as dist
+from torch import Tensor, nn
+
+from .models.llama import Llama, LlamaConfig, lm_loss, muon_and_adam_params
+from .optim import Muon
+
+
+def build_llama(
+    cfg: LlamaConfig,
+    device: torch.device,
+    dtype: torch.dtype = torch.bfloat16,
+    mesh=None,
+    seed: int | None = 0,
+    block_factory=None,
+) -> Llama:
+    """Build a randomly initialised Llama on ``device`` without a host copy.
+
+    With ``mesh`` (a 1-D DeviceMesh) every decoder block and the root are
+    wrapped with FSDP2 ``fully_shard`` (dim-0 sharding of every parameter).
+    """
+    with torch.device("meta"):
+        model = Llama(cfg, block_factory=block_factory).to(dtype)
+    if mesh is not None:
+        from torch.distributed.fsdp import fully_shard
+
+        for layer in model.layers:
+            fully_shard(layer, mesh=mesh)
+        fully_shard(model, mesh=mesh)
+    model.to_empty(device=device)
+    if seed is not None:
+        torch.manual_seed(seed + (dist.get_rank() if dist.is_initialized() else 0))
+    model.init_weights()
+    return model
+
+
+def build_optimizer(model: nn.Module, optimizer_cls=Muon, lr: float = 1e-3, wd: float = 0.1,
+                    adam_lr: float | None = None, muon_group: dict | None = None, **kwargs):
+    """Muon on the 2-D / 3-D decoder weights, AdamW on embeddings, norms and head."""
+    muon, adam = muon_and_adam_params(model)
+    groups = [dict(params=muon, **(muon_group or {}))]
+    if adam:
+        g = {"params": adam, "algorithm": "adamw"}
+        if adam_lr is not None:
+            g["lr"] = adam_lr
+        groups.append(g)
+    return optimizer_cls(groups, lr=lr, wd=wd, **kwargs)
+
+
+def synthetic_batch(batch: int, seq: int, vocab: int, generator: torch.Generator | None = None,
+                    pin: bool = False) -> tuple[Tensor, Tensor]:
+    """Uniform random token ids; targets are the next token."""
+    ids = torch.randint(0, vocab, (batch, seq + 1), generator=generator)
+    if pin:
+        ids = ids.pin_memory()
+    return ids[:, :-1], ids[:, 1:]
+
+
+class Trainer:
+    """forward -> loss -> backward -> optimizer.step -> zero_grad."""
+
+    def __init__(self, model: nn.Module, optimizer: torch.optim.Optimizer):
+        self.model = model
+        self.optimizer = optimizer
+
+    def forward_backward(self, tokens: Tensor, targets: Tensor) -> Tensor:
+        loss = lm_loss(self.model(tokens), targets)
+        loss.backward()
+        return loss.detach()
+
+    def step(self, tokens: Tensor, targets: Tensor) -> Tensor:
+        loss = self.forward_backward(tokens, targets)
+        self.optimizer.step()
+        self.optimizer.zero_grad(set_to_none=True)
+        return loss

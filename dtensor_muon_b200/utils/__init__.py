@@ -1,0 +1,4 @@
+from .dtensor import to_local
+from .foreach import group_tensors_by_shape, move_tensors_to_device
+
+__all__ = ["to_local", "group_tensors_by_shape", "move_tensors_to_device"]
