@@ -183,8 +183,12 @@ def build_reference(args, world, device):
                 dim = b.numel() * 2
                 b.copy_(1.0 / (shapes["rope_theta"] ** (torch.arange(0, dim, 2, device=device).float() / dim)))
     muon_p, adam_p = hidden_and_rest(model)
+    # batch_size=32: the reference's Triton gram_nd computes the batch offset
+    # pid_b * stride_xb in 32-bit; one stacked batch of all 64 gate/up matrices
+    # (64 x 4096 x 14336 > 2**31 elements) overflows it and faults. 32 matrices
+    # per batch stay below 2**31 elements for every Llama-3-8B shape group.
     opt = RefMuon([{"params": muon_p}, {"params": adam_p, "algorithm": "adamw"}], lr=args.lr, wd=0.1,
-                  orthogonalization_strategy=args.strategy)
+                  orthogonalization_strategy=args.strategy, batch_size=args.ref_batch_size)
 
     def step(tokens, targets):
         logits = model(input_ids=tokens).logits
@@ -208,6 +212,8 @@ def main():
     ap.add_argument("--lr", type=float, default=1e-3)
     ap.add_argument("--strategy", default="polar_express")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--ref-batch-size", type=int, default=32,
+                    help="reference arm: Muon foreach batch_size (keeps its Gram kernel below 2**31 elements)")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
