@@ -21,7 +21,10 @@
 #include <c10/cuda/CUDAGuard.h>
 #include <torch/extension.h>
 
+#include <mutex>
+
 #include "common.cuh"
+#include "no_alloc.h"
 
 namespace dmb {
 
@@ -391,4 +394,88 @@ at::Tensor normuon_finalize(const at::Tensor& rowsq, const at::Tensor& v_ptrs, i
   return scale;
 }
 
+// ------------------------------------------------------------------------
+// Allocation-free variant of muon_pack (no momentum) + norm_finalize; see
+// no_alloc.h. The pointer table and the partial sums live in this array.
+namespace {
+
+constexpr size_t kNoAllocPtrBytes = sizeof(int64_t) * kNoAllocMaxBatch;
+constexpr size_t kNoAllocScratchBytes = kNoAllocPtrBytes + sizeof(float) * (size_t)kNoAllocMaxPartials;
+
+static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratchBytes];
+
+__global__ void noalloc_fill_ptrs(int64_t base, int64_t stride_bytes, int batch) {
+  int64_t* table = reinterpret_cast<int64_t*>(g_noalloc_scratch);
+  for (int b = blockIdx.x * blockDim.x + threadIdx.x; b < batch; b += gridDim.x * blockDim.x)
+    table[b] = base + (int64_t)b * stride_bytes;
+}
+
+// Per-device address of g_noalloc_scratch, looked up once with that device current.
+unsigned char* noalloc_scratch_ptr(int dev, cudaError_t* err) {
+  static unsigned char* addr[64] = {nullptr};
+  static std::mutex mu;
+  std::lock_guard<std::mutex> lock(mu);
+  *err = cudaSuccess;
+  if (dev < 0 || dev >= 64) {
+    *err = cudaErrorInvalidDevice;
+    return nullptr;
+  }
+  if (!addr[dev]) {
+    void* p = nullptr;
+    cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+    if (e != cudaSuccess) {
+      *err = e;
+      return nullptr;
+    }
+    addr[dev] = static_cast<unsigned char*>(p);
+  }
+  return addr[dev];
+}
+
+}  // namespace
 }  // namespace dmb
+
+extern "C" int dmb_pack_normalize_noalloc(const void* src, int src_dtype, int batch, int R, int C, int Np, int Mp,
+                                          float fac, float eps, void* out_ws, float* inv_norm,
+                                          cudaStream_t stream) {
+  using namespace dmb;
+  if (!src || !out_ws || !inv_norm || batch <= 0 || R <= 0 || C <= 0) return -1;
+  if (src_dtype != 0 && src_dtype != 1) return -1;
+  if (Np % TILE != 0 || Mp % TILE != 0) return -1;
+  const bool transpose = R > C;
+  const int N = transpose ? C : R, M = transpose ? R : C;
+  if (N > Np || M > Mp) return -1;
+  const long long tiles = (long long)(Np / TILE) * (Mp / TILE);
+  if (batch > kNoAllocMaxBatch || tiles * batch > (long long)kNoAllocMaxPartials) return -1;
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return (int)e;
+  unsigned char* scratch = noalloc_scratch_ptr(dev, &e);
+  if (!scratch) return (int)e;
+  int64_t* ptrs = reinterpret_cast<int64_t*>(scratch);
+  float* partial = reinterpret_cast<float*>(scratch + kNoAllocPtrBytes);
+
+  const int64_t esize = src_dtype == 0 ? 4 : 2;
+  noalloc_fill_ptrs<<<(batch + 255) / 256, 256, 0, stream>>>(reinterpret_cast<int64_t>(src), (int64_t)R * C * esize,
+                                                              batch);
+  PackArgs a{};
+  a.src = ptrs;
+  a.buf = nullptr;
+  a.src_dtype = src_dtype;
+  a.R = R;
+  a.C = C;
+  a.ld = C;
+  a.transpose = transpose ? 1 : 0;
+  a.Np = Np;
+  a.Mp = Mp;
+  a.momentum = 0.f;
+  a.nesterov = 0;
+  a.maximize = 0;
+  a.out = reinterpret_cast<__nv_bfloat16*>(out_ws);
+  a.partial = partial;
+  a.tiles_c = Mp / TILE;
+  muon_pack_kernel<<<dim3((unsigned)tiles, batch), PACK_THREADS, 0, stream>>>(a);
+  norm_finalize_kernel<<<batch, 256, 0, stream>>>(partial, (int)tiles, fac, eps, inv_norm, nullptr);
+  return (int)cudaGetLastError();
+}
+
