@@ -26,6 +26,9 @@ _LAUNCHES = {
     "lp_momentum_step": 1,
     "lp_dequantize": 1,
     "lp_quantize": 1,
+    "dist_pack": 2,
+    "dist_apply": 1,
+    "dist_barrier": 1,
 }
 launch_count = 0
 

@@ -39,6 +39,13 @@ at::Tensor lp_dequantize(const at::Tensor& codes, const at::Tensor& scale, const
 void lp_quantize(const at::Tensor& x, at::Tensor codes, at::Tensor scale, const at::Tensor& qmap, int64_t fmt,
                  int64_t block);
 
+// ---- dist_ops.cu
+void dist_pack(const at::Tensor& meta_i64, const at::Tensor& meta_i32, const at::Tensor& peer_base,
+               std::vector<int64_t> ints, std::vector<double> floats, bool has_buf, bool has_var);
+void dist_apply(const at::Tensor& meta_i64, const at::Tensor& meta_i32, const at::Tensor& peer_base,
+                std::vector<int64_t> ints, std::vector<double> floats, bool has_var);
+void dist_barrier(const at::Tensor& flag_base, int64_t rank, int64_t world, int64_t epoch);
+
 // One status word per device. Kernels whose bounded waits give up write an
 // error code here; the host reads and clears it with take_device_error().
 int* device_error_word(int dev) {
@@ -81,5 +88,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("lp_momentum_step", &dmb::lp_momentum_step);
   m.def("lp_dequantize", &dmb::lp_dequantize);
   m.def("lp_quantize", &dmb::lp_quantize);
+  m.def("dist_pack", &dmb::dist_pack);
+  m.def("dist_apply", &dmb::dist_apply);
+  m.def("dist_barrier", &dmb::dist_barrier);
   m.def("take_device_error", &dmb::take_device_error);
 }

@@ -1,0 +1,319 @@
+// Owner-compute Muon for dim-0 (FSDP) sharded 2-D matrices over NVLink peer memory.
+//
+// The reference moves whole matrices to "owner" ranks with a DTensor
+// redistribute (an NCCL all-to-all), orthogonalises there and redistributes
+// back (src/muonium/orthogonalize/orthogonalize.py:140-155, call sites C4/C5).
+// Here both all-to-alls are fused into the memory-bound kernels around the
+// owner's GEMMs, through a symmetric buffer every rank can address:
+//
+//   dist_pack_rows    local momentum / Nesterov on this rank's row shard,
+//                     bf16 cast, (transpose,) zero padding, written with P2P
+//                     stores straight into the owner's orthogonalisation
+//                     workspace (+ per-block partial sums of squares, local)
+//   dist_push_sums    per-matrix sum of the partials -> owner's sums[slot][rank]
+//                     (and, for NorMuon, this rank's variance rows -> owner)
+//   dist_barrier      device-side barrier on flags in the symmetric buffer;
+//                     every wait is bounded (error word + return, no hang)
+//   dist_apply_rows   P2P loads of this rank's rows of the owner's result
+//                     (+ NorMuon row scale), cautious / plain WD, lr step on
+//                     the local shard, NorMuon variance rows copied back
+//
+// The owner itself runs the ordinary local engine (norm_finalize,
+// ortho_iterate, row_sumsq / normuon_finalize) on its slots in between.
+#include <ATen/cuda/CUDAContext.h>
+#include <c10/cuda/CUDAGuard.h>
+#include <torch/extension.h>
+
+#include "common.cuh"
+
+namespace dmb {
+
+int* device_error_word(int dev);
+
+namespace {
+
+constexpr int T = 64;
+constexpr int NT = 256;
+
+__device__ __forceinline__ float ldf(const void* p, int dt, long long i) {
+  return dt == 0 ? reinterpret_cast<const float*>(p)[i] : __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(p)[i]);
+}
+__device__ __forceinline__ void stf(void* p, int dt, long long i, float v) {
+  if (dt == 0)
+    reinterpret_cast<float*>(p)[i] = v;
+  else
+    reinterpret_cast<__nv_bfloat16*>(p)[i] = __float2bfloat16_rn(v);
+}
+
+struct DistArgs {
+  const int64_t* grad;  // [B] local shard pointers (rows_local x C)
+  const int64_t* buf;   // [B] local fp32 momentum shard pointers
+  const int64_t* param; // [B] local param shard pointers
+  const int64_t* var;   // [B] local NorMuon variance rows (fp32, rows_local) or nullptr
+  const int* owner;     // [B]
+  const int* slot;      // [B]
+  const int64_t* peer_base;  // [W] symmetric buffer base on every rank
+  long long x_off, res_off, sums_off, vbuf_off, rs_off;  // byte offsets of regions
+  int grad_dtype, param_dtype;
+  int R, C, transpose, Np, Mp;
+  int r0, r1;           // this rank's global rows [r0, r1)
+  int g1;               // rows handled by pack: [r0, g1) (last rank covers padding)
+  int rank, world;
+  float momentum;
+  int nesterov, maximize;
+  float* partial;       // [B, nblk] local
+  int tiles_c;
+  float lr_eff, wd;
+  int cautious, has_rowscale;
+};
+
+__device__ __forceinline__ float block_sum(float v, float* red) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  const int w = threadIdx.x >> 5, l = threadIdx.x & 31;
+  __syncthreads();
+  if (l == 0) red[w] = v;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    float s = 0.f;
+    for (int i = 0; i < NT / 32; ++i) s += red[i];
+    red[0] = s;
+  }
+  __syncthreads();
+  return red[0];
+}
+
+// Tile (64 rows of [r0, g1)) x (64 source columns of [0, Cpad)).
+__global__ void __launch_bounds__(NT) dist_pack_rows_kernel(const DistArgs a) {
+  __shared__ float tile[T][T + 1];
+  __shared__ float red[NT / 32];
+  const int b = blockIdx.y;
+  const int tr = blockIdx.x / a.tiles_c, tc = blockIdx.x % a.tiles_c;
+  const int g0 = a.r0 + tr * T, c0 = tc * T;
+  const void* g = reinterpret_cast<const void*>(a.grad[b]);
+  float* buf = a.buf ? reinterpret_cast<float*>(a.buf[b]) : nullptr;
+  const int j = threadIdx.x & (T - 1), i0 = threadIdx.x >> 6;
+  float ss = 0.f;
+  for (int i = i0; i < T; i += NT / T) {
+    const int gr = g0 + i, c = c0 + j;
+    float v = 0.f;
+    if (gr < a.r1 && c < a.C) {
+      const long long idx = (long long)(gr - a.r0) * a.C + c;
+      float gv = ldf(g, a.grad_dtype, idx);
+      if (a.maximize) gv = -gv;
+      if (buf) {
+        const float m = fmaf(buf[idx], a.momentum, gv);
+        buf[idx] = m;
+        v = a.nesterov ? fmaf(m, a.momentum, gv) : m;
+      } else {
+        v = gv;
+      }
+      v = __bfloat162float(__float2bfloat16_rn(v));
+      ss = fmaf(v, v, ss);
+    }
+    tile[i][j] = v;
+  }
+  __syncthreads();
+  __nv_bfloat16* X = reinterpret_cast<__nv_bfloat16*>(a.peer_base[a.owner[b]] + a.x_off) +
+                     (long long)a.slot[b] * a.Np * a.Mp;
+  const int Cpad = a.transpose ? a.Np : a.Mp;
+  if (!a.transpose) {
+    // X[gr][c]: row-contiguous stores.
+    for (int i = i0; i < T; i += NT / T) {
+      const int gr = g0 + i, c = c0 + j;
+      if (gr < a.g1 && c < Cpad) X[(long long)gr * a.Mp + c] = __float2bfloat16_rn(tile[i][j]);
+    }
+  } else {
+    // X[c][gr]: consecutive threads walk gr.
+    for (int i = i0; i < T; i += NT / T) {
+      const int c = c0 + i, gr = g0 + j;
+      if (gr < a.g1 && c < Cpad) X[(long long)c * a.Mp + gr] = __float2bfloat16_rn(tile[j][i]);
+    }
+  }
+  const float tot = block_sum(ss, red);
+  if (threadIdx.x == 0) a.partial[(long long)b * gridDim.x + blockIdx.x] = tot;
+}
+
+__global__ void __launch_bounds__(NT) dist_push_sums_kernel(const DistArgs a, int nblk) {
+  __shared__ float red[NT / 32];
+  const int b = blockIdx.x;
+  float s = 0.f;
+  for (int i = threadIdx.x; i < nblk; i += NT) s += a.partial[(long long)b * nblk + i];
+  const float tot = block_sum(s, red);
+  const int64_t base = a.peer_base[a.owner[b]];
+  if (threadIdx.x == 0) reinterpret_cast<float*>(base + a.sums_off)[(long long)a.slot[b] * a.world + a.rank] = tot;
+  if (a.var) {
+    const float* v = reinterpret_cast<const float*>(a.var[b]);
+    float* dst = reinterpret_cast<float*>(base + a.vbuf_off) + (long long)a.slot[b] * a.R;
+    for (int r = a.r0 + threadIdx.x; r < a.r1; r += NT) dst[r] = v[r - a.r0];
+  }
+}
+
+__global__ void __launch_bounds__(NT) dist_apply_rows_kernel(const DistArgs a) {
+  __shared__ float tile[T][T + 1];
+  const int b = blockIdx.y;
+  const int tr = blockIdx.x / a.tiles_c, tc = blockIdx.x % a.tiles_c;
+  const int g0 = a.r0 + tr * T, c0 = tc * T;
+  const int64_t base = a.peer_base[a.owner[b]];
+  const __nv_bfloat16* U = reinterpret_cast<const __nv_bfloat16*>(base + a.res_off) + (long long)a.slot[b] * a.Np * a.Mp;
+  const float* rs = a.has_rowscale ? reinterpret_cast<const float*>(base + a.rs_off) + (long long)a.slot[b] * a.R : nullptr;
+  const int j = threadIdx.x & (T - 1), i0 = threadIdx.x >> 6;
+  if (!a.transpose) {
+    for (int i = i0; i < T; i += NT / T) {
+      const int gr = g0 + i, c = c0 + j;
+      tile[i][j] = (gr < a.r1 && c < a.C) ? __bfloat162float(U[(long long)gr * a.Mp + c]) : 0.f;
+    }
+  } else {
+    for (int i = i0; i < T; i += NT / T) {
+      const int c = c0 + i, gr = g0 + j;
+      tile[j][i] = (gr < a.r1 && c < a.C) ? __bfloat162float(U[(long long)c * a.Mp + gr]) : 0.f;
+    }
+  }
+  __syncthreads();
+  void* P = reinterpret_cast<void*>(a.param[b]);
+  for (int i = i0; i < T; i += NT / T) {
+    const int gr = g0 + i, c = c0 + j;
+    if (gr >= a.r1 || c >= a.C) continue;
+    float u = tile[i][j];
+    if (rs) u *= rs[gr];
+    const long long idx = (long long)(gr - a.r0) * a.C + c;
+    const float pv = ldf(P, a.param_dtype, idx);
+    if (a.wd != 0.f) {
+      if (a.cautious) {
+        if (u * pv > 0.f) u = fmaf(a.wd, pv, u);
+      } else {
+        u = fmaf(a.wd, pv, u);
+      }
+    }
+    stf(P, a.param_dtype, idx, fmaf(-a.lr_eff, u, pv));
+  }
+  // NorMuon: this rank's rows of the updated variance come back from the owner.
+  if (a.var && tc == 0) {
+    const float* vsrc = reinterpret_cast<const float*>(base + a.vbuf_off) + (long long)a.slot[b] * a.R;
+    float* v = reinterpret_cast<float*>(a.var[b]);
+    for (int i = threadIdx.x; i < T; i += NT) {
+      const int gr = g0 + i;
+      if (gr < a.r1) v[gr - a.r0] = vsrc[gr];
+    }
+  }
+}
+
+// flags: uint32 [world] at offset 0 of every rank's flag buffer. Rank r
+// announces epoch e by writing flags[r] = e on every peer, then waits until
+// its own flags[k] >= e for all k. Bounded: gives up after kWaitTimeoutNs.
+__global__ void dist_barrier_kernel(const int64_t* flag_base, int rank, int world, unsigned epoch, int* err) {
+  const int k = threadIdx.x;
+  if (k < world) {
+    __threadfence_system();
+    unsigned* peer = reinterpret_cast<unsigned*>(flag_base[k]) + rank;
+    asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(peer), "r"(epoch) : "memory");
+    const unsigned* mine = reinterpret_cast<const unsigned*>(flag_base[rank]) + k;
+    const unsigned long long t0 = global_timer_ns();
+    while (true) {
+      unsigned v;
+      asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(mine) : "memory");
+      if ((int)(v - epoch) >= 0) break;
+      if (global_timer_ns() - t0 > kWaitTimeoutNs) {
+        atomicExch(err, (int)kErrPeerTimeout);
+        break;
+      }
+      __nanosleep(64);
+    }
+  }
+  __syncthreads();
+  __threadfence_system();
+}
+
+}  // namespace
+
+namespace {
+DistArgs make_args(const at::Tensor& meta_i64, const at::Tensor& meta_i32, const at::Tensor& peer_base,
+                   const std::vector<int64_t>& ints, const std::vector<double>& floats, bool has_buf,
+                   bool has_var) {
+  // meta_i64: [4, B] grad, buf, param, var pointers; meta_i32: [2, B] owner, slot.
+  const int B = meta_i64.size(1);
+  DistArgs a{};
+  const int64_t* m = meta_i64.data_ptr<int64_t>();
+  a.grad = m;
+  a.buf = has_buf ? m + B : nullptr;
+  a.param = m + 2 * B;
+  a.var = has_var ? m + 3 * B : nullptr;
+  a.owner = meta_i32.data_ptr<int>();
+  a.slot = meta_i32.data_ptr<int>() + B;
+  a.peer_base = peer_base.data_ptr<int64_t>();
+  // ints: x_off res_off sums_off vbuf_off rs_off grad_dtype param_dtype R C transpose Np Mp r0 r1 g1 rank world
+  //       nesterov maximize cautious has_rowscale
+  a.x_off = ints[0];
+  a.res_off = ints[1];
+  a.sums_off = ints[2];
+  a.vbuf_off = ints[3];
+  a.rs_off = ints[4];
+  a.grad_dtype = ints[5];
+  a.param_dtype = ints[6];
+  a.R = ints[7];
+  a.C = ints[8];
+  a.transpose = ints[9];
+  a.Np = ints[10];
+  a.Mp = ints[11];
+  a.r0 = ints[12];
+  a.r1 = ints[13];
+  a.g1 = ints[14];
+  a.rank = ints[15];
+  a.world = ints[16];
+  a.nesterov = ints[17];
+  a.maximize = ints[18];
+  a.cautious = ints[19];
+  a.has_rowscale = ints[20];
+  a.momentum = floats[0];
+  a.lr_eff = floats[1];
+  a.wd = floats[2];
+  return a;
+}
+}  // namespace
+
+// Phase 1: local momentum + P2P scatter into owners' workspaces, then per-matrix
+// sums (and NorMuon variance rows) pushed to the owners.
+void dist_pack(const at::Tensor& meta_i64, const at::Tensor& meta_i32, const at::Tensor& peer_base,
+               std::vector<int64_t> ints, std::vector<double> floats, bool has_buf, bool has_var) {
+  const at::cuda::CUDAGuard guard(meta_i64.device());
+  DistArgs a = make_args(meta_i64, meta_i32, peer_base, ints, floats, has_buf, has_var);
+  const int B = meta_i64.size(1);
+  const int Cpad = a.transpose ? a.Np : a.Mp;
+  a.tiles_c = (Cpad + T - 1) / T;
+  const int rows = a.g1 - a.r0;
+  const int tiles_r = rows > 0 ? (rows + T - 1) / T : 0;
+  const int nblk = tiles_r * a.tiles_c;
+  auto partial = at::zeros({B, std::max(nblk, 1)}, meta_i64.options().dtype(at::kFloat));
+  a.partial = partial.data_ptr<float>();
+  auto st = at::cuda::getCurrentCUDAStream();
+  if (nblk > 0) {
+    dist_pack_rows_kernel<<<dim3(nblk, B), NT, 0, st>>>(a);
+    C10_CUDA_KERNEL_LAUNCH_CHECK();
+  }
+  dist_push_sums_kernel<<<B, NT, 0, st>>>(a, std::max(nblk, 1));
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+// Phase 3: P2P gather of this rank's rows of the owners' results + apply.
+void dist_apply(const at::Tensor& meta_i64, const at::Tensor& meta_i32, const at::Tensor& peer_base,
+                std::vector<int64_t> ints, std::vector<double> floats, bool has_var) {
+  const at::cuda::CUDAGuard guard(meta_i64.device());
+  DistArgs a = make_args(meta_i64, meta_i32, peer_base, ints, floats, false, has_var);
+  const int B = meta_i64.size(1);
+  a.tiles_c = (a.C + T - 1) / T;
+  const int rows = a.r1 - a.r0;
+  if (rows <= 0) return;
+  const int tiles_r = (rows + T - 1) / T;
+  dist_apply_rows_kernel<<<dim3(tiles_r * a.tiles_c, B), NT, 0, at::cuda::getCurrentCUDAStream()>>>(a);
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+void dist_barrier(const at::Tensor& flag_base, int64_t rank, int64_t world, int64_t epoch) {
+  const at::cuda::CUDAGuard guard(flag_base.device());
+  TORCH_CHECK(world <= 1024);
+  dist_barrier_kernel<<<1, (int)((world + 31) / 32 * 32), 0, at::cuda::getCurrentCUDAStream()>>>(
+      flag_base.data_ptr<int64_t>(), (int)rank, (int)world, (unsigned)epoch, device_error_word(flag_base.get_device()));
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+}  // namespace dmb

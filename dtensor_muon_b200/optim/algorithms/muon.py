@@ -28,6 +28,39 @@ def fused_path_ok(params, grads, buffers, split_sizes) -> bool:
     return split_sizes is None and base._seams_are_builtin() and muon_fused.native_eligible(params, grads, buffers)
 
 
+def distributed_fused(params, grads, buffers, lr_ratios, lr, split_sizes, ns_steps, kw, variances=None) -> bool:
+    """Run the fused distributed path when the batch qualifies; returns whether it ran.
+
+    * 2-D FSDP (Shard(0)) DTensors: owner-compute over symmetric memory.
+    * 3-D DTensors sharded only on dim 0: the local shards are whole matrices,
+      so the single-GPU fused kernels run on them with no communication.
+    """
+    if split_sizes is not None or ns_steps < 1 or not base._seams_are_builtin():
+        return False
+    if not params or not hasattr(grads[0], "device_mesh"):
+        return False
+    from ...parallel import owner_compute
+
+    effs = lr_effs(lr, lr_ratios)
+    if owner_compute.eligible(params, grads, buffers, variances):
+        owner_compute.owner_compute_update(params, grads, buffers, effs, ns_steps=ns_steps, variances=variances, **kw)
+        return True
+    if owner_compute.fsdp3d_local_eligible(params, grads, buffers) and (
+        variances is None or all(hasattr(v, "to_local") for v in variances)
+    ):
+        muon_fused.fused_muon_update(
+            [p.to_local() for p in params],
+            [g.to_local() for g in grads],
+            [b.to_local() for b in buffers],
+            effs,
+            ns_steps=ns_steps,
+            variances=[v.to_local() for v in variances] if variances is not None else None,
+            **kw,
+        )
+        return True
+    return False
+
+
 def lr_effs(lr: Tensor, lr_ratios: list[Tensor]) -> list[float]:
     lr_f = float(lr)
     return [float(r) * lr_f for r in lr_ratios]
@@ -138,6 +171,10 @@ class MuonBaseline(MuonAlgorithm):
                 ns_steps=ns_steps,
                 strategy=orthogonalization_strategy,
             )
+            return
+        kw = dict(weight_decay=weight_decay, cautious_wd=cautious_wd, momentum=momentum, nesterov=nesterov,
+                  maximize=maximize, strategy=orthogonalization_strategy)
+        if distributed_fused(params, grads, bufs, lr_ratios, lr, split_sizes, ns_steps, kw):
             return
         g = list(torch._foreach_neg(grads)) if maximize else list(grads)
         torch._foreach_mul_(bufs, momentum)

@@ -23,7 +23,13 @@ from .base import (
     orthogonalize_single,
     register_muon_algorithm,
 )
-from .muon import apply_weight_decay_and_step, foreach_weight_decay_and_step, fused_path_ok, lr_effs
+from .muon import (
+    apply_weight_decay_and_step,
+    distributed_fused,
+    foreach_weight_decay_and_step,
+    fused_path_ok,
+    lr_effs,
+)
 
 
 def _normuon_normalize(
@@ -149,6 +155,10 @@ class NorMuon(MuonAlgorithm):
                 variances=variances,
                 muon_beta2=muon_beta2,
             )
+            return
+        kw = dict(weight_decay=weight_decay, cautious_wd=cautious_wd, momentum=momentum, nesterov=nesterov,
+                  maximize=maximize, strategy=orthogonalization_strategy, muon_beta2=muon_beta2)
+        if distributed_fused(params, grads, bufs, lr_ratios, lr, split_sizes, ns_steps, kw, variances=variances):
             return
         g = list(torch._foreach_neg(grads)) if maximize else list(grads)
         torch._foreach_mul_(bufs, momentum)

@@ -464,6 +464,12 @@ class Muon(torch.optim.Optimizer):
             return
         lr = group["lr"]
         wd = group["wd"]
+        # Adam is elementwise: DTensors that share placements update through their local shards.
+        if all(hasattr(t, "to_local") for t in params + grads + m1 + m2 + mx):
+            places = {tuple(t.placements) for t in params + grads + m1 + m2 + mx}
+            if len(places) == 1:
+                params, grads = [t.to_local() for t in params], [t.to_local() for t in grads]
+                m1, m2, mx = [t.to_local() for t in m1], [t.to_local() for t in m2], [t.to_local() for t in mx]
         grad_scale = getattr(self, "grad_scale", None)
         found_inf = getattr(self, "found_inf", None)
         use_native = (

@@ -1,0 +1,98 @@
+"""Symmetric (peer-addressable) device memory for the fused collective kernels.
+
+Every rank allocates a buffer of the same size; after a rendezvous each rank
+knows every peer's base address and the kernels in ``ops/csrc/dist_ops.cu``
+read and write peers' buffers directly with P2P loads / stores over NVLink /
+NVSwitch. ``torch.distributed._symmetric_memory`` is used only as the
+allocator + address-exchange bootstrap; the data movement and the barrier are
+our own kernels. Barriers are bounded on the device (2 s) and report through
+the per-device error word, which :meth:`SymmetricWorkspace.check` raises on.
+"""
+
+from __future__ import annotations
+
+import os
+
+import torch
+import torch.distributed as dist
+
+from ..ops import _ext
+
+
+def available() -> bool:
+    if os.environ.get("DMB_DISABLE_SYMM", "0") == "1":
+        return False
+    if not (dist.is_available() and dist.is_initialized()):
+        return False
+    try:
+        import torch.distributed._symmetric_memory  # noqa: F401
+    except ImportError:
+        return False
+    return _ext.available()
+
+
+class SymmetricWorkspace:
+    """A grow-only symmetric byte buffer plus a persistent barrier flag array."""
+
+    def __init__(self, group: dist.ProcessGroup, device: torch.device):
+        import torch.distributed._symmetric_memory as symm_mem
+
+        self._symm = symm_mem
+        self.group = group
+        self.device = device
+        self.rank = dist.get_rank(group)
+        self.world = dist.get_world_size(group)
+        name = group.group_name
+        enable = getattr(symm_mem, "enable_symm_mem_for_group", None)
+        if enable is not None:
+            try:
+                enable(name)
+            except Exception:  # already enabled / not needed on this version
+                pass
+        self._flags = symm_mem.empty(max(64, self.world), dtype=torch.int32, device=device)
+        self._flags.zero_()
+        hdl = symm_mem.rendezvous(self._flags, name)
+        self.flag_ptrs = torch.tensor(list(hdl.buffer_ptrs), dtype=torch.int64).to(device)
+        torch.cuda.synchronize(device)
+        dist.barrier(group)
+        self.epoch = 0
+        self._buf: torch.Tensor | None = None
+        self.peer_base: torch.Tensor | None = None
+        self._keep = [hdl]
+
+    def barrier(self) -> None:
+        """Device-side barrier over the group (bounded wait in the kernel)."""
+        self.epoch = (self.epoch + 1) & 0x7FFFFFFF
+        _ext.load().dist_barrier(self.flag_ptrs, self.rank, self.world, self.epoch)
+
+    def buffer(self, nbytes: int) -> tuple[torch.Tensor, torch.Tensor]:
+        """Local view of at least ``nbytes`` symmetric bytes and the [world] tensor of peer base addresses.
+
+        Growing is collective: every rank must request the same sizes in the same order.
+        """
+        if self._buf is None or self._buf.numel() < nbytes:
+            if self._buf is not None:
+                self.barrier()  # peers are done with the old buffer
+            size = max(nbytes, int((self._buf.numel() if self._buf is not None else 0) * 1.25))
+            size = (size + (1 << 20) - 1) // (1 << 20) * (1 << 20)
+            buf = self._symm.empty(size, dtype=torch.uint8, device=self.device)
+            hdl = self._symm.rendezvous(buf, self.group.group_name)
+            self.peer_base = torch.tensor(list(hdl.buffer_ptrs), dtype=torch.int64).to(self.device)
+            self._buf = buf
+            self._keep.append(hdl)
+        return self._buf, self.peer_base
+
+    def check(self) -> None:
+        _ext.check_device_errors(self.device)
+
+
+_WORKSPACES: dict[tuple[str, int], SymmetricWorkspace] = {}
+
+
+def workspace_for(group: dist.ProcessGroup, device: torch.device) -> SymmetricWorkspace:
+    key = (group.group_name, device.index if device.index is not None else torch.cuda.current_device())
+    ws = _WORKSPACES.get(key)
+    if ws is None:
+        ws = SymmetricWorkspace(group, device)
+        _WORKSPACES[key] = ws
+    return ws

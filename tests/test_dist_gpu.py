@@ -1,0 +1,62 @@
+"""Fused owner-compute path (FSDP-sharded 2-D DTensors over NVLink peer memory)
+against the single-process optimizer, on 2 GPUs (mirrors the reference's
+tests/optim/test_optim_foreach.py:318-391)."""
+
+import pytest
+import torch
+
+from testkit import assert_close, run_distributed
+
+pytestmark = [pytest.mark.gpu, pytest.mark.multigpu]
+
+SHAPES = [(256, 512), (512, 256), (200, 384), (384, 200), (64, 96), (1024, 4096)]
+
+
+def _worker(rank, world, algorithm, strategy, n_steps, dtype_name):
+    import torch
+    from torch.distributed.device_mesh import init_device_mesh
+    from torch.distributed.tensor import Shard, distribute_tensor
+
+    from dtensor_muon_b200 import Muon
+    from dtensor_muon_b200.ops import _ext
+
+    dtype = getattr(torch, dtype_name)
+    device = torch.device("cuda", rank)
+    mesh = init_device_mesh("cuda", (world,))
+    gen = torch.Generator().manual_seed(0)
+    fulls = [torch.randn(s, generator=gen).to(dtype) for s in SHAPES for _ in range(3)]
+    ref_params = [torch.nn.Parameter(f.clone().to(device)) for f in fulls]
+    dist_params = [torch.nn.Parameter(distribute_tensor(f.clone().to(device), mesh, [Shard(0)])) for f in fulls]
+    kw = dict(lr=0.05, wd=0.1, orthogonalization_strategy=strategy)
+    ref = Muon([{"params": ref_params, "algorithm": algorithm}], foreach=True, **kw)
+    opt = Muon([{"params": dist_params, "algorithm": algorithm}], foreach=True, **kw)
+    for _ in range(n_steps):
+        grads = [torch.randn(f.shape, generator=gen).to(dtype) for f in fulls]
+        for p, g in zip(ref_params, grads):
+            p.grad = g.to(device)
+        for p, g in zip(dist_params, grads):
+            p.grad = distribute_tensor(g.to(device), mesh, [Shard(0)])
+        ref.step()
+        opt.step()
+    torch.cuda.synchronize()
+    _ext.check_device_errors(device)
+    for i, (r, d) in enumerate(zip(ref_params, dist_params)):
+        assert_close(d.full_tensor(), r.detach(), rtol=1e-2, atol=3e-2, max_mismatch_pct=1.0, msg=f"param {i}")
+        if algorithm == "normuon":
+            assert_close(
+                opt.state[d]["variance_neuron"].full_tensor(), ref.state[r]["variance_neuron"], rtol=2e-2, atol=1e-6
+            )
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+@pytest.mark.parametrize("algorithm", ["muon", "normuon"])
+@pytest.mark.parametrize("strategy", ["polar_express", "newton_schulz"])
+def test_owner_compute_matches_single_process(algorithm, strategy):
+    run_distributed(
+        _worker, 2, args=(algorithm, strategy, 3, "float32"), backend="nccl", device_type="cuda", timeout_s=120
+    )
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+def test_owner_compute_bf16_params():
+    run_distributed(_worker, 2, args=("muon", "polar_express", 2, "bfloat16"), backend="nccl", device_type="cuda")
