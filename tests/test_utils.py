@@ -62,8 +62,11 @@ def test_spawner_sets_env_and_collectives_work():
 
 
 def _failing_worker(rank, world):
+    import time
+
     if rank == 1:
         raise RuntimeError("rank one failed on purpose")
+    time.sleep(10)  # the healthy rank outlives the failure, so the failure is what surfaces
 
 
 def test_spawner_propagates_worker_failure():
