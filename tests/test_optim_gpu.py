@@ -82,7 +82,9 @@ def test_native_adam_matches_torch(amsgrad, algorithm, dtype):
     g = torch.Generator().manual_seed(0)
     shapes = [(7,), (33, 5), (1000,)]
     a = [nn.Parameter(torch.randn(s, generator=g).cuda().to(dtype)) for s in shapes]
-    b = [nn.Parameter(t.detach().clone()) for t in a]
+    # fp32 reference: the native kernel does fp32 math with one rounding per
+    # state write, while torch's bf16 path rounds after every sub-step.
+    b = [nn.Parameter(t.detach().clone().float()) for t in a]
     opt = Muon([{"params": a, "algorithm": algorithm, "lr": 0.01, "wd": 0.1, "amsgrad": amsgrad}])
     cls = torch.optim.AdamW if algorithm == "adamw" else torch.optim.Adam
     ref = cls(b, lr=0.01, weight_decay=0.1, betas=(0.9, 0.95), amsgrad=amsgrad, foreach=False)
@@ -90,13 +92,13 @@ def test_native_adam_matches_torch(amsgrad, algorithm, dtype):
     for _ in range(3):
         for x, y in zip(a, b):
             gr = torch.randn(x.shape, generator=g).cuda().to(dtype)
-            x.grad, y.grad = gr.clone(), gr.clone()
+            x.grad, y.grad = gr.clone(), gr.clone().float()
         opt.step()
         ref.step()
     assert _ext.launch_count - n0 == 3, "native AdamW kernel must run once per step"
-    tol = dict(rtol=1e-5, atol=1e-6) if dtype == torch.float32 else dict(rtol=1e-2, atol=1e-2)
+    tol = dict(rtol=1e-5, atol=1e-6) if dtype == torch.float32 else dict(rtol=2e-2, atol=2e-2)
     for x, y in zip(a, b):
-        torch.testing.assert_close(x, y, **tol)
+        torch.testing.assert_close(x.float(), y.detach(), **tol)
 
 
 @pytest.mark.parametrize("cls", [Muon8bit, Muon4bit, MuonFp8])
