@@ -29,6 +29,8 @@ _LAUNCHES = {
     "dist_pack": 2,
     "dist_apply": 1,
     "dist_barrier": 1,
+    "ep_scatter_rows": 1,
+    "ep_gather_rows": 1,
 }
 launch_count = 0
 

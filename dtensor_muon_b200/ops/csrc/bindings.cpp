@@ -46,6 +46,12 @@ void dist_apply(const at::Tensor& meta_i64, const at::Tensor& meta_i32, const at
                 std::vector<int64_t> ints, std::vector<double> floats, bool has_var);
 void dist_barrier(const at::Tensor& flag_base, int64_t rank, int64_t world, int64_t epoch);
 
+// ---- ep_ops.cu
+void ep_scatter_rows(const at::Tensor& src, const at::Tensor& dst_rank, const at::Tensor& dst_row,
+                     const at::Tensor& peer_base, int64_t off);
+void ep_gather_rows(at::Tensor& dst, const at::Tensor& src_rank, const at::Tensor& src_row,
+                    const at::Tensor& peer_base, int64_t off);
+
 // One status word per device. Kernels whose bounded waits give up write an
 // error code here; the host reads and clears it with take_device_error().
 int* device_error_word(int dev) {
@@ -91,5 +97,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("dist_pack", &dmb::dist_pack);
   m.def("dist_apply", &dmb::dist_apply);
   m.def("dist_barrier", &dmb::dist_barrier);
+  m.def("ep_scatter_rows", &dmb::ep_scatter_rows);
+  m.def("ep_gather_rows", &dmb::ep_gather_rows);
   m.def("take_device_error", &dmb::take_device_error);
 }
