@@ -128,6 +128,10 @@ class MuonBaseline(MuonAlgorithm):
                 strategy=orthogonalization_strategy,
             )
             return
+        kw = dict(weight_decay=weight_decay, cautious_wd=cautious_wd, momentum=momentum, nesterov=nesterov,
+                  maximize=maximize, strategy=orthogonalization_strategy)
+        if distributed_fused([param], [grad], [buf], [lr_ratio], lr, split_sizes, ns_steps, kw):
+            return
         g32 = (-grad if maximize else grad).to(torch.float32)
         new_buf = buf.to(torch.float32) * momentum + g32
         buf.copy_(new_buf)

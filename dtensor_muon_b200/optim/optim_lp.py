@@ -195,6 +195,8 @@ class MuonLP(Muon):
 
     #: quantisation format of the subclass; None keeps fp32 buffers
     _fmt: int | None = None
+    #: tensors dequantised at once on the generic path (bounds the fp32 temporaries)
+    _LP_CHUNK = 8
 
     def __init__(
         self,
@@ -274,28 +276,40 @@ class MuonLP(Muon):
         if not quant_keys:
             return super().muon(algorithm, params, grads, state, lr_ratios, **kw)
         opts = {k: v for k, v in kw.items() if k not in ("foreach",)}
+        pending: dict[tuple, list[int]] = {}
         for i, (p, g, r) in enumerate(zip(params, grads, lr_ratios, strict=True)):
             st = {k: v[i] for k, v in state.items()}
             if self._fused_lp(algorithm, p, g, st, r, opts):
                 continue
-            # Generic: dequantise into fp32 temporaries, normal update, requantise.
-            temps = {}
-            for k in quant_keys:
-                q = st[k]
-                if isinstance(q, QuantizedState):
-                    t = q.dequantize()
-                    if isinstance(g, DTensor):
-                        t = DTensor.from_local(
-                            t, device_mesh=g.device_mesh, placements=g.placements, run_check=False,
-                            shape=g.shape, stride=g.stride(),
-                        )
-                    temps[k] = (q, t)
-                    st[k] = t
-            super().muon(
-                algorithm, [p], [g], {k: [v] for k, v in st.items()}, [r], foreach=False, **opts
-            )
-            for k, (q, t) in temps.items():
-                q.copy_(to_local(t))
+            pending.setdefault((tuple(g.shape), g.dtype, str(g.device)), []).append(i)
+        # Generic: dequantise into fp32 temporaries, run the normal (batched when
+        # on CUDA) update for a bounded chunk of same-shape tensors, requantise.
+        for idxs in pending.values():
+            for s in range(0, len(idxs), self._LP_CHUNK):
+                sel = idxs[s : s + self._LP_CHUNK]
+                temps: list[tuple[QuantizedState, Tensor]] = []
+                sub = {k: [] for k in state}
+                for i in sel:
+                    g = grads[i]
+                    for k in state:
+                        q = state[k][i]
+                        if isinstance(q, QuantizedState):
+                            t = q.dequantize()
+                            if isinstance(g, DTensor):
+                                t = DTensor.from_local(
+                                    t, device_mesh=g.device_mesh, placements=g.placements, run_check=False,
+                                    shape=g.shape, stride=g.stride(),
+                                )
+                            temps.append((q, t))
+                            q = t
+                        sub[k].append(q)
+                on_cuda = all(to_local(params[i]).is_cuda for i in sel)
+                super().muon(
+                    algorithm, [params[i] for i in sel], [grads[i] for i in sel], sub,
+                    [lr_ratios[i] for i in sel], foreach=on_cuda, **opts,
+                )
+                for q, t in temps:
+                    q.copy_(to_local(t))
 
     def _fused_lp(self, algorithm, p, g, st, lr_ratio, opts) -> bool:
         q = st.get("momentum_buffer")
@@ -303,15 +317,22 @@ class MuonLP(Muon):
             return False
         if type(algorithm) not in (MuonBaseline, NorMuon) or not algo_base._seams_are_builtin():
             return False
-        if opts.get("split_sizes") is not None or isinstance(p, DTensor) or isinstance(g, DTensor):
+        if opts.get("split_sizes") is not None:
             return False
+        if isinstance(p, DTensor) or isinstance(g, DTensor):
+            # Dim-0-sharded 3-D stacks (EP experts): local shards are whole matrices.
+            from ..orthogonalize import is_fsdp_3d_sharded
+
+            if not (isinstance(p, DTensor) and is_fsdp_3d_sharded([g])):
+                return False
+            p, g = p.to_local(), g.to_local()
         if not (p.is_contiguous() and g.is_contiguous() and _ext.available()):
             return False
         if p.dtype not in (torch.float32, torch.bfloat16) or g.dtype not in (torch.float32, torch.bfloat16):
             return False
         variances = None
         if isinstance(algorithm, NorMuon):
-            v = st["variance_neuron"]
+            v = to_local(st["variance_neuron"])
             if isinstance(v, QuantizedState) or not (v.is_cuda and v.is_contiguous()):
                 return False
             variances = [v]
