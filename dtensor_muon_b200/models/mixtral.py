@@ -17,6 +17,7 @@ import torch
 import torch.nn.functional as F
 from torch import Tensor, nn
 
+from ..ops import model_ops as _model_ops
 from .llama import Block, Llama, LlamaConfig
 
 
@@ -54,7 +55,7 @@ def _grouped(x: Tensor, w: Tensor, counts: Tensor) -> Tensor:
 
 def expert_ffn(x: Tensor, counts: Tensor, w1: Tensor, w3: Tensor, w2: Tensor) -> Tensor:
     """SwiGLU experts over expert-grouped rows."""
-    h = F.silu(_grouped(x, w1, counts)) * _grouped(x, w3, counts)
+    h = _model_ops.swiglu(_grouped(x, w1, counts), _grouped(x, w3, counts))
     return _grouped(h, w2, counts)
 
 

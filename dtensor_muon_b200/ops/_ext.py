@@ -31,6 +31,9 @@ _LAUNCHES = {
     "dist_barrier": 1,
     "ep_scatter_rows": 1,
     "ep_gather_rows": 1,
+    "rope": 1,
+    "swiglu_fwd": 1,
+    "swiglu_bwd": 1,
 }
 launch_count = 0
 

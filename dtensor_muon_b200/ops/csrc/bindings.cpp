@@ -52,6 +52,11 @@ void ep_scatter_rows(const at::Tensor& src, const at::Tensor& dst_rank, const at
 void ep_gather_rows(at::Tensor& dst, const at::Tensor& src_rank, const at::Tensor& src_row,
                     const at::Tensor& peer_base, int64_t off);
 
+// ---- model_ops.cu
+at::Tensor rope(const at::Tensor& x, const at::Tensor& cos_t, const at::Tensor& sin_t, double sign);
+at::Tensor swiglu_fwd(const at::Tensor& a, const at::Tensor& b);
+std::vector<at::Tensor> swiglu_bwd(const at::Tensor& a, const at::Tensor& b, const at::Tensor& dh);
+
 // One status word per device. Kernels whose bounded waits give up write an
 // error code here; the host reads and clears it with take_device_error().
 int* device_error_word(int dev) {
@@ -99,5 +104,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("dist_barrier", &dmb::dist_barrier);
   m.def("ep_scatter_rows", &dmb::ep_scatter_rows);
   m.def("ep_gather_rows", &dmb::ep_gather_rows);
+  m.def("rope", &dmb::rope);
+  m.def("swiglu_fwd", &dmb::swiglu_fwd);
+  m.def("swiglu_bwd", &dmb::swiglu_bwd);
   m.def("take_device_error", &dmb::take_device_error);
 }

@@ -1,0 +1,42 @@
+"""Fused RoPE / SwiGLU kernels against fp32 PyTorch (forward and backward)."""
+
+import pytest
+import torch
+import torch.nn.functional as F
+
+from dtensor_muon_b200.models.llama import rope_tables
+from dtensor_muon_b200.ops import _ext, model_ops
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.mark.parametrize("shape", [(2, 64, 4, 128), (1, 33, 8, 64), (1, 4096, 8, 128)])
+def test_rope_fwd_bwd(shape):
+    torch.manual_seed(0)
+    cos, sin = rope_tables(shape[-1], shape[1], 10000.0, "cuda")
+    x = torch.randn(shape, device="cuda").bfloat16().requires_grad_()
+    xr = x.detach().float().requires_grad_()
+    n0 = _ext.launch_count
+    y = model_ops.rope(x, cos, sin)
+    yr = model_ops.rope_reference(xr, cos, sin)
+    torch.testing.assert_close(y.float(), yr, rtol=1e-2, atol=1e-2)
+    g = torch.randn(shape, device="cuda")
+    y.backward(g.bfloat16())
+    yr.backward(g)
+    torch.testing.assert_close(x.grad.float(), xr.grad, rtol=1e-2, atol=2e-2)
+    assert _ext.launch_count - n0 == 2
+
+
+def test_swiglu_fwd_bwd():
+    torch.manual_seed(1)
+    a = torch.randn(257, 384, device="cuda").bfloat16().requires_grad_()
+    b = torch.randn(257, 384, device="cuda").bfloat16().requires_grad_()
+    ar, br = a.detach().float().requires_grad_(), b.detach().float().requires_grad_()
+    h = model_ops.swiglu(a, b)
+    hr = F.silu(ar) * br
+    torch.testing.assert_close(h.float(), hr, rtol=1e-2, atol=1e-2)
+    g = torch.randn_like(hr)
+    h.backward(g.bfloat16())
+    hr.backward(g)
+    torch.testing.assert_close(a.grad.float(), ar.grad, rtol=2e-2, atol=3e-2)
+    torch.testing.assert_close(b.grad.float(), br.grad, rtol=2e-2, atol=3e-2)
