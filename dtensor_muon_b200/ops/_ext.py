@@ -16,6 +16,8 @@ _IMPORT_ERROR: Exception | None = None
 _LAUNCHES = {
     "gram_sym": 1,
     "gemm_ax": 1,
+    "gram_sym2": 1,
+    "gemm_ax2": 1,
     "muon_pack": 1,
     "norm_finalize": 1,
     "muon_apply": 1,

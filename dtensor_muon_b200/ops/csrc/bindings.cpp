@@ -16,6 +16,14 @@ void gemm_ax(const at::Tensor& a, const at::Tensor& x, at::Tensor& out, const c1
              int64_t res_pow, int64_t max_ctas);
 at::Tensor ortho_iterate(at::Tensor x, at::Tensor x2, at::Tensor a_ws, at::Tensor b_ws, const at::Tensor& inv_norm,
                          const at::Tensor& coeffs, int64_t max_ctas);
+void gram_sym2(const at::Tensor& x, at::Tensor& out, const c10::optional<at::Tensor>& res,
+               const c10::optional<at::Tensor>& scale, double coef_acc, double coef_res, int64_t acc_pow,
+               int64_t res_pow);
+void gemm_ax2(const at::Tensor& a, const at::Tensor& x, at::Tensor& out, const c10::optional<at::Tensor>& res,
+              const c10::optional<at::Tensor>& scale, double coef_acc, double coef_res, int64_t acc_pow,
+              int64_t res_pow);
+void set_gemm_variant(int64_t v);
+int64_t get_gemm_variant();
 // ---- muon_ops.cu
 at::Tensor muon_pack(const at::Tensor& src_ptrs, const c10::optional<at::Tensor>& buf_ptrs, int64_t src_dtype_code,
                      int64_t R, int64_t C, int64_t ld, bool transpose, at::Tensor& out, double momentum,
@@ -89,6 +97,10 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gram_sym", &dmb::gram_sym);
   m.def("gemm_ax", &dmb::gemm_ax);
   m.def("ortho_iterate", &dmb::ortho_iterate);
+  m.def("gram_sym2", &dmb::gram_sym2);
+  m.def("gemm_ax2", &dmb::gemm_ax2);
+  m.def("set_gemm_variant", &dmb::set_gemm_variant);
+  m.def("get_gemm_variant", &dmb::get_gemm_variant);
   m.def("muon_pack", &dmb::muon_pack);
   m.def("norm_finalize", &dmb::norm_finalize);
   m.def("muon_apply", &dmb::muon_apply);

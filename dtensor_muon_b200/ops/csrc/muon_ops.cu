@@ -196,6 +196,168 @@ __global__ void __launch_bounds__(PACK_THREADS) muon_apply_kernel(const ApplyArg
   }
 }
 
+
+// ---- vectorised variants (16-byte accesses; need C % 8 == 0) -------------
+__device__ __forceinline__ void ld8(const void* base, int dt, long long idx, float (&v)[8]) {
+  if (dt == 0) {
+    const float4* p = reinterpret_cast<const float4*>(reinterpret_cast<const float*>(base) + idx);
+    const float4 x = p[0], y = p[1];
+    v[0] = x.x; v[1] = x.y; v[2] = x.z; v[3] = x.w; v[4] = y.x; v[5] = y.y; v[6] = y.z; v[7] = y.w;
+  } else {
+    const uint4 u = *reinterpret_cast<const uint4*>(reinterpret_cast<const __nv_bfloat16*>(base) + idx);
+    const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      v[2 * k] = bf16_bits_to_float((uint16_t)(w[k] & 0xFFFFu));
+      v[2 * k + 1] = bf16_bits_to_float((uint16_t)(w[k] >> 16));
+    }
+  }
+}
+
+__device__ __forceinline__ void st8(void* base, int dt, long long idx, const float (&v)[8]) {
+  if (dt == 0) {
+    float4* p = reinterpret_cast<float4*>(reinterpret_cast<float*>(base) + idx);
+    p[0] = make_float4(v[0], v[1], v[2], v[3]);
+    p[1] = make_float4(v[4], v[5], v[6], v[7]);
+  } else {
+    *reinterpret_cast<uint4*>(reinterpret_cast<__nv_bfloat16*>(base) + idx) =
+        make_uint4(pack_bf16x2(v[0], v[1]), pack_bf16x2(v[2], v[3]), pack_bf16x2(v[4], v[5]), pack_bf16x2(v[6], v[7]));
+  }
+}
+
+// g' for 8 consecutive elements (momentum update in place when buf != null); returns bf16-rounded values.
+__device__ __forceinline__ void momentum8(const PackArgs& a, const void* src, float* buf, long long idx, float (&v)[8]) {
+  ld8(src, a.src_dtype, idx, v);
+  if (a.maximize)
+#pragma unroll
+    for (int k = 0; k < 8; ++k) v[k] = -v[k];
+  if (buf) {
+    float m[8];
+    ld8(buf, 0, idx, m);
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      m[k] = fmaf(m[k], a.momentum, v[k]);
+      v[k] = a.nesterov ? fmaf(m[k], a.momentum, v[k]) : m[k];
+    }
+    st8(buf, 0, idx, m);
+  }
+#pragma unroll
+  for (int k = 0; k < 8; ++k) v[k] = __bfloat162float(__float2bfloat16_rn(v[k]));
+}
+
+// Non-transposed: tile 16 rows x 128 cols, 8 elements per thread.
+__global__ void __launch_bounds__(PACK_THREADS) muon_pack_rows_vec(const PackArgs a) {
+  __shared__ float red[PACK_THREADS / 32];
+  const int b = blockIdx.y;
+  const int tr = blockIdx.x / a.tiles_c, tc = blockIdx.x % a.tiles_c;
+  const int r = tr * 16 + (threadIdx.x >> 4), c = tc * 128 + (threadIdx.x & 15) * 8;
+  float v[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+  float ss = 0.f;
+  if (r < a.R && c < a.C) {
+    float* buf = a.buf ? reinterpret_cast<float*>(a.buf[b]) : nullptr;
+    momentum8(a, reinterpret_cast<const void*>(a.src[b]), buf, (long long)r * a.ld + c, v);
+#pragma unroll
+    for (int k = 0; k < 8; ++k) ss = fmaf(v[k], v[k], ss);
+  }
+  st8(a.out + (long long)b * a.Np * a.Mp, 1, (long long)r * a.Mp + c, v);
+  const float tot = block_sum<PACK_THREADS>(ss, red);
+  if (threadIdx.x == 0) a.partial[(long long)b * gridDim.x + blockIdx.x] = tot;
+}
+
+// Transposed: 64 x 64 tile through shared memory, 16-byte loads and stores.
+__global__ void __launch_bounds__(PACK_THREADS) muon_pack_tr_vec(const PackArgs a) {
+  __shared__ float tile[TILE][TILE + 1];
+  __shared__ float red[PACK_THREADS / 32];
+  const int b = blockIdx.y;
+  const int wt_r = blockIdx.x / a.tiles_c, wt_c = blockIdx.x % a.tiles_c;
+  const int wr0 = wt_r * TILE, wc0 = wt_c * TILE;  // workspace rows = source cols
+  const int sr0 = wc0, sc0 = wr0;
+  const void* src = reinterpret_cast<const void*>(a.src[b]);
+  float* buf = a.buf ? reinterpret_cast<float*>(a.buf[b]) : nullptr;
+  const int lane8 = (threadIdx.x & 7) * 8, row = threadIdx.x >> 3;
+  float ss = 0.f;
+#pragma unroll
+  for (int it = 0; it < 2; ++it) {
+    const int sr = row + it * 32;
+    const int r = sr0 + sr, c = sc0 + lane8;
+    float v[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+    if (r < a.R && c < a.C) {
+      momentum8(a, src, buf, (long long)r * a.ld + c, v);
+#pragma unroll
+      for (int k = 0; k < 8; ++k) ss = fmaf(v[k], v[k], ss);
+    }
+#pragma unroll
+    for (int k = 0; k < 8; ++k) tile[sr][lane8 + k] = v[k];
+  }
+  __syncthreads();
+  __nv_bfloat16* out = a.out + (long long)b * a.Np * a.Mp;
+#pragma unroll
+  for (int it = 0; it < 2; ++it) {
+    const int wr = row + it * 32;  // source column offset
+    float v[8];
+#pragma unroll
+    for (int k = 0; k < 8; ++k) v[k] = tile[lane8 + k][wr];
+    st8(out, 1, (long long)(wr0 + wr) * a.Mp + wc0 + lane8, v);
+  }
+  const float tot = block_sum<PACK_THREADS>(ss, red);
+  if (threadIdx.x == 0) a.partial[(long long)b * gridDim.x + blockIdx.x] = tot;
+}
+
+__device__ __forceinline__ void apply8(const ApplyArgs& a, int b, int r, int c, float (&u)[8]) {
+  const float rs = (a.rowscale ? a.rowscale[(long long)b * a.R + r] : 1.f) * (a.mat_scale ? a.mat_scale[b] : 1.f);
+  void* dst = reinterpret_cast<void*>(a.dst[b]);
+  const long long idx = (long long)r * a.ld + c;
+  float p[8];
+  ld8(dst, a.dst_dtype, idx, p);
+#pragma unroll
+  for (int k = 0; k < 8; ++k) {
+    float x = u[k] * rs;
+    if (a.wd != 0.f) {
+      if (!a.cautious || x * p[k] > 0.f) x = fmaf(a.wd, p[k], x);
+    }
+    p[k] = fmaf(-a.lr_eff, x, p[k]);
+  }
+  st8(dst, a.dst_dtype, idx, p);
+}
+
+__global__ void __launch_bounds__(PACK_THREADS) muon_apply_rows_vec(const ApplyArgs a) {
+  const int b = blockIdx.y;
+  const int tr = blockIdx.x / a.tiles_c, tc = blockIdx.x % a.tiles_c;
+  const int r = tr * 16 + (threadIdx.x >> 4), c = tc * 128 + (threadIdx.x & 15) * 8;
+  if (r >= a.R || c >= a.C) return;
+  float u[8];
+  ld8(a.ws + (long long)b * a.Np * a.Mp, 1, (long long)r * a.Mp + c, u);
+  apply8(a, b, r, c, u);
+}
+
+__global__ void __launch_bounds__(PACK_THREADS) muon_apply_tr_vec(const ApplyArgs a) {
+  __shared__ float tile[TILE][TILE + 1];
+  const int b = blockIdx.y;
+  const int pt_r = blockIdx.x / a.tiles_c, pt_c = blockIdx.x % a.tiles_c;
+  const int r0 = pt_r * TILE, c0 = pt_c * TILE;  // param tile; workspace rows = param cols
+  const __nv_bfloat16* ws = a.ws + (long long)b * a.Np * a.Mp;
+  const int lane8 = (threadIdx.x & 7) * 8, row = threadIdx.x >> 3;
+#pragma unroll
+  for (int it = 0; it < 2; ++it) {
+    const int wr = row + it * 32;
+    float v[8];
+    ld8(ws, 1, (long long)(c0 + wr) * a.Mp + r0 + lane8, v);
+#pragma unroll
+    for (int k = 0; k < 8; ++k) tile[wr][lane8 + k] = v[k];
+  }
+  __syncthreads();
+#pragma unroll
+  for (int it = 0; it < 2; ++it) {
+    const int i = row + it * 32;
+    const int r = r0 + i, c = c0 + lane8;
+    if (r >= a.R || c >= a.C) continue;
+    float u[8];
+#pragma unroll
+    for (int k = 0; k < 8; ++k) u[k] = tile[lane8 + k][i];
+    apply8(a, b, r, c, u);
+  }
+}
+
 // rowsq[b, r] = sum_c u[b, r, c]^2 with u read from the (possibly transposed) workspace.
 __global__ void __launch_bounds__(256) row_sumsq_rows_kernel(const __nv_bfloat16* ws, int Np, int Mp, int R, int C,
                                                              float* rowsq) {
@@ -297,8 +459,22 @@ at::Tensor muon_pack(const at::Tensor& src_ptrs, const c10::optional<at::Tensor>
   a.out = reinterpret_cast<__nv_bfloat16*>(out.data_ptr());
   a.partial = partial.data_ptr<float>();
   a.tiles_c = tiles_c;
+  auto st = at::cuda::getCurrentCUDAStream();
+  if (C % 8 == 0 && ld % 8 == 0) {
+    if (!transpose) {
+      a.tiles_c = Mp / 128;
+      auto p2 = at::empty({B, (Np / 16) * a.tiles_c}, out.options().dtype(at::kFloat));
+      a.partial = p2.data_ptr<float>();
+      muon_pack_rows_vec<<<dim3((Np / 16) * a.tiles_c, B), PACK_THREADS, 0, st>>>(a);
+      C10_CUDA_KERNEL_LAUNCH_CHECK();
+      return p2;
+    }
+    muon_pack_tr_vec<<<dim3(tiles_r * tiles_c, B), PACK_THREADS, 0, st>>>(a);
+    C10_CUDA_KERNEL_LAUNCH_CHECK();
+    return partial;
+  }
   dim3 grid(tiles_r * tiles_c, B);
-  muon_pack_kernel<<<grid, PACK_THREADS, 0, at::cuda::getCurrentCUDAStream()>>>(a);
+  muon_pack_kernel<<<grid, PACK_THREADS, 0, st>>>(a);
   C10_CUDA_KERNEL_LAUNCH_CHECK();
   return partial;
 }
@@ -335,9 +511,21 @@ void muon_apply(const at::Tensor& ws, bool transpose, int64_t R, int64_t C, int6
   a.wd = (float)wd;
   a.cautious = cautious;
   a.mode = 0;
+  auto st = at::cuda::getCurrentCUDAStream();
+  if (C % 8 == 0 && ld % 8 == 0) {
+    if (!transpose) {
+      a.tiles_c = (C + 127) / 128;
+      muon_apply_rows_vec<<<dim3(((R + 15) / 16) * a.tiles_c, B), PACK_THREADS, 0, st>>>(a);
+    } else {
+      a.tiles_c = (C + TILE - 1) / TILE;
+      muon_apply_tr_vec<<<dim3(((R + TILE - 1) / TILE) * a.tiles_c, B), PACK_THREADS, 0, st>>>(a);
+    }
+    C10_CUDA_KERNEL_LAUNCH_CHECK();
+    return;
+  }
   a.tiles_c = (C + TILE - 1) / TILE;
   dim3 grid(((R + TILE - 1) / TILE) * a.tiles_c, B);
-  muon_apply_kernel<<<grid, PACK_THREADS, 0, at::cuda::getCurrentCUDAStream()>>>(a);
+  muon_apply_kernel<<<grid, PACK_THREADS, 0, st>>>(a);
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 

@@ -366,6 +366,19 @@ void check_ws(const at::Tensor& t, const char* name) {
 }  // namespace
 
 int* device_error_word(int dev);
+void gram_sym2(const at::Tensor& x, at::Tensor& out, const c10::optional<at::Tensor>& res,
+               const c10::optional<at::Tensor>& scale, double coef_acc, double coef_res, int64_t acc_pow,
+               int64_t res_pow);
+void gemm_ax2(const at::Tensor& a, const at::Tensor& x, at::Tensor& out, const c10::optional<at::Tensor>& res,
+              const c10::optional<at::Tensor>& scale, double coef_acc, double coef_res, int64_t acc_pow,
+              int64_t res_pow);
+
+CUtensorMap make_bf16_map_3d(const at::Tensor& t, int box_cols, int box_rows) { return make_map(t, box_cols, box_rows); }
+
+// 0: 1-SM kernels (128 x 256 tiles); 1 (default): 2-SM cta_group::2 kernels (256 x 256 per CTA pair).
+static int g_gemm_variant = 1;
+void set_gemm_variant(int64_t v) { g_gemm_variant = (int)v; }
+int64_t get_gemm_variant() { return g_gemm_variant; }
 
 // out[b] = coef_acc * s_b^acc_pow * x[b] x[b]^T  (+ coef_res * s_b^res_pow * res[b])
 // x: [B, N, K]; out, res: [B, N, N]. Symmetric store.
@@ -465,9 +478,15 @@ at::Tensor ortho_iterate(at::Tensor x, at::Tensor x2, at::Tensor a_ws, at::Tenso
   for (int s = 0; s < steps; ++s) {
     const bool first = (s == 0);
     c10::optional<at::Tensor> sc = first ? c10::optional<at::Tensor>(inv_norm) : c10::nullopt;
-    gram_sym(cur, a_ws, c10::nullopt, sc, 1.0, 0.0, first ? 2 : 0, 0, max_ctas);
-    gram_sym(a_ws, b_ws, a_ws, c10::nullopt, c[s][2], c[s][1], 0, 0, max_ctas);
-    gemm_ax(b_ws, cur, nxt, cur, sc, 1.0, c[s][0], first ? 1 : 0, first ? 1 : 0, max_ctas);
+    if (g_gemm_variant == 1) {
+      gram_sym2(cur, a_ws, c10::nullopt, sc, 1.0, 0.0, first ? 2 : 0, 0);
+      gram_sym2(a_ws, b_ws, a_ws, c10::nullopt, c[s][2], c[s][1], 0, 0);
+      gemm_ax2(b_ws, cur, nxt, cur, sc, 1.0, c[s][0], first ? 1 : 0, first ? 1 : 0);
+    } else {
+      gram_sym(cur, a_ws, c10::nullopt, sc, 1.0, 0.0, first ? 2 : 0, 0, max_ctas);
+      gram_sym(a_ws, b_ws, a_ws, c10::nullopt, c[s][2], c[s][1], 0, 0, max_ctas);
+      gemm_ax(b_ws, cur, nxt, cur, sc, 1.0, c[s][0], first ? 1 : 0, first ? 1 : 0, max_ctas);
+    }
     std::swap(cur, nxt);
   }
   return cur;

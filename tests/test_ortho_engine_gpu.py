@@ -70,3 +70,47 @@ def test_orthogonalize_steps0_is_normalized_input():
     got = torch.stack(ortho.orthogonalize_native(list(g.unbind(0)), 0, "newton_schulz", 1e-7))
     ref = g / (g.norm(dim=(-2, -1), keepdim=True) + 1e-7)
     torch.testing.assert_close(got.float(), ref, rtol=1e-2, atol=1e-3)
+
+
+# ---- 2-SM (cta_group::2) kernels ------------------------------------------
+@pytest.mark.parametrize("shape", [(1, 256, 256), (2, 512, 768), (3, 1024, 2048)])
+def test_gram2_matches_fp32(shape):
+    torch.manual_seed(5)
+    C = _ext.load()
+    x = torch.randn(*shape, device="cuda").bfloat16()
+    out = torch.empty(shape[0], shape[1], shape[1], device="cuda", dtype=torch.bfloat16)
+    C.gram_sym2(x, out, None, None, 1.0, 0.0, 0, 0)
+    ref = x.float() @ x.float().mT
+    torch.testing.assert_close(out.float(), ref, rtol=2e-2, atol=2e-2 * shape[-1] ** 0.5)
+    assert torch.equal(out, out.mT)
+    _ext.check_device_errors("cuda")
+
+
+@pytest.mark.parametrize("B,N,M", [(1, 256, 256), (2, 512, 768), (2, 1024, 2048)])
+def test_gemm_ax2_matches_fp32(B, N, M):
+    torch.manual_seed(6)
+    C = _ext.load()
+    a = torch.randn(B, N, N, device="cuda").bfloat16()
+    x = torch.randn(B, N, M, device="cuda").bfloat16()
+    out = torch.empty_like(x)
+    C.gemm_ax2(a, x, out, x, None, 0.5, -1.5, 0, 0)
+    ref = 0.5 * (a.float() @ x.float()) - 1.5 * x.float()
+    torch.testing.assert_close(out.float(), ref, rtol=2e-2, atol=3e-2 * N**0.5)
+    _ext.check_device_errors("cuda")
+
+
+@pytest.mark.parametrize("strategy", ["newton_schulz", "polar_express"])
+def test_orthogonalize_2sm_matches_1sm(strategy):
+    C = _ext.load()
+    torch.manual_seed(7)
+    g = torch.randn(3, 384, 1000, device="cuda")
+    prev = C.get_gemm_variant()
+    try:
+        C.set_gemm_variant(0)
+        one = torch.stack(ortho.orthogonalize_native(list(g.unbind(0)), 5, strategy, 1e-7))
+        C.set_gemm_variant(1)
+        two = torch.stack(ortho.orthogonalize_native(list(g.unbind(0)), 5, strategy, 1e-7))
+    finally:
+        C.set_gemm_variant(prev)
+    assert _close_frac(two, one, rtol=1e-2, atol=3e-2) < 0.01
+    _ext.check_device_errors("cuda")
