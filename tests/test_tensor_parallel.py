@@ -1,0 +1,52 @@
+"""Tensor-parallel Llama + NorMuon on a TP group (gloo, CPU) against one process."""
+
+import torch
+
+from testkit import run_distributed
+
+
+def _worker(rank, world):
+    import torch
+    from torch.distributed.device_mesh import init_device_mesh
+
+    from dtensor_muon_b200 import Muon
+    from dtensor_muon_b200.models.llama import Llama, lm_loss, muon_and_adam_params, preset
+    from dtensor_muon_b200.parallel.tensor_parallel import apply_tensor_parallel
+
+    cfg = preset("tiny")
+    torch.manual_seed(0)
+    ref = Llama(cfg)
+    ref.init_weights(seed=0)
+    model = Llama(cfg)
+    model.load_state_dict(ref.state_dict())
+    mesh = init_device_mesh("cpu", (world,))
+    apply_tensor_parallel(model, mesh)
+
+    def make_opt(m):
+        mu, ad = muon_and_adam_params(m)
+        return Muon([{"params": mu, "algorithm": "normuon"}, {"params": ad, "algorithm": "adamw"}],
+                    lr=0.02, orthogonalization_strategy="newton_schulz")
+
+    o_ref, o_tp = make_opt(ref), make_opt(model)
+    gen = torch.Generator().manual_seed(3)
+    for _ in range(2):
+        tok = torch.randint(0, cfg.vocab_size, (2, 17), generator=gen)
+        l_ref = lm_loss(ref(tok[:, :-1]), tok[:, 1:])
+        l_tp = lm_loss(model(tok[:, :-1]), tok[:, 1:])
+        torch.testing.assert_close(l_tp, l_ref, rtol=1e-4, atol=1e-4)
+        l_ref.backward()
+        l_tp.backward()
+        o_ref.step()
+        o_tp.step()
+        o_ref.zero_grad()
+        o_tp.zero_grad()
+    refp = dict(ref.named_parameters())
+    for name, p in model.named_parameters():
+        full = p.full_tensor() if hasattr(p, "full_tensor") else p
+        # bf16 orthogonalisation on different reduction orders: bf16-level budget
+        bad = (~torch.isclose(full.detach(), refp[name].detach(), rtol=1e-2, atol=3e-3)).float().mean().item()
+        assert bad < 0.02, (name, bad)
+
+
+def test_tp_normuon_matches_single_process_gloo():
+    run_distributed(_worker, 2)
