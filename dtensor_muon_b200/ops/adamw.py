@@ -64,6 +64,8 @@ def fused_adam(
         dts = _CODE[p.dtype] | (_CODE[g.dtype] << 4) | (_CODE[m.dtype] << 8) | (_CODE[v.dtype] << 12) | (
             _CODE[vmax.dtype] << 16
         )
+        if p.numel() % 8 == 0 and all(t.data_ptr() % 16 == 0 for t in (p, g, m, v, vmax)):
+            dts |= 1 << 20  # 16-byte vector path
         rows.append(
             [
                 p.data_ptr(),

@@ -193,3 +193,33 @@ __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
 }
 
 }  // namespace dmb
+
+namespace dmb {
+// 8 consecutive elements of an fp32 (dt 0) or bf16 (dt 1) array as fp32; idx % 8 == 0 and 16-byte aligned base.
+__device__ __forceinline__ void load8(const void* base, int dt, long long idx, float (&v)[8]) {
+  if (dt == 0) {
+    const float4* p = reinterpret_cast<const float4*>(reinterpret_cast<const float*>(base) + idx);
+    const float4 x = p[0], y = p[1];
+    v[0] = x.x; v[1] = x.y; v[2] = x.z; v[3] = x.w; v[4] = y.x; v[5] = y.y; v[6] = y.z; v[7] = y.w;
+  } else {
+    const uint4 u = *reinterpret_cast<const uint4*>(reinterpret_cast<const __nv_bfloat16*>(base) + idx);
+    const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      v[2 * k] = bf16_bits_to_float((uint16_t)(w[k] & 0xFFFFu));
+      v[2 * k + 1] = bf16_bits_to_float((uint16_t)(w[k] >> 16));
+    }
+  }
+}
+
+__device__ __forceinline__ void store8(void* base, int dt, long long idx, const float (&v)[8]) {
+  if (dt == 0) {
+    float4* p = reinterpret_cast<float4*>(reinterpret_cast<float*>(base) + idx);
+    p[0] = make_float4(v[0], v[1], v[2], v[3]);
+    p[1] = make_float4(v[4], v[5], v[6], v[7]);
+  } else {
+    *reinterpret_cast<uint4*>(reinterpret_cast<__nv_bfloat16*>(base) + idx) =
+        make_uint4(pack_bf16x2(v[0], v[1]), pack_bf16x2(v[2], v[3]), pack_bf16x2(v[4], v[5]), pack_bf16x2(v[6], v[7]));
+  }
+}
+}  // namespace dmb
