@@ -128,7 +128,7 @@ def build_ours(args, world, device):
         from torch.distributed.device_mesh import init_device_mesh
 
         mesh = init_device_mesh("cuda", (world,))
-    model = build_llama(cfg, device, mesh=mesh, seed=0)
+    model = build_llama(cfg, device, mesh=mesh, seed=0, fsdp_comm=args.fsdp_comm)
     opt = build_optimizer(model, Muon, lr=args.lr, wd=0.1, orthogonalization_strategy=args.strategy)
     from dtensor_muon_b200.models.llama import lm_loss
 
@@ -218,6 +218,8 @@ def main():
     ap.add_argument("--lr", type=float, default=1e-3)
     ap.add_argument("--strategy", default="polar_express")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--fsdp-comm", default=os.environ.get("DMB_FSDP_COMM", "p2p"), choices=["p2p", "nccl"],
+                    help="ours: FSDP collectives on NVLink P2P kernels or NCCL")
     ap.add_argument("--ref-batch-size", type=int, default=32,
                     help="reference arm: Muon foreach batch_size (keeps its Gram kernel below 2**31 elements)")
     args = ap.parse_args()

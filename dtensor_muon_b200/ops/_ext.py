@@ -31,6 +31,8 @@ _LAUNCHES = {
     "dist_pack": 2,
     "dist_apply": 1,
     "dist_barrier": 1,
+    "fsdp_all_gather_pull": 1,
+    "fsdp_reduce_scatter_pull": 1,
     "ep_scatter_rows": 1,
     "ep_gather_rows": 1,
     "rope": 1,

@@ -53,6 +53,10 @@ void dist_pack(const at::Tensor& meta_i64, const at::Tensor& meta_i32, const at:
 void dist_apply(const at::Tensor& meta_i64, const at::Tensor& meta_i32, const at::Tensor& peer_base,
                 std::vector<int64_t> ints, std::vector<double> floats, bool has_var);
 void dist_barrier(const at::Tensor& flag_base, int64_t rank, int64_t world, int64_t epoch);
+void fsdp_all_gather_pull(at::Tensor& out, const at::Tensor& peer_base, int64_t off, int64_t in_bytes, int64_t world,
+                          int64_t max_ctas);
+void fsdp_reduce_scatter_pull(at::Tensor& out, const at::Tensor& peer_base, int64_t off, int64_t rank, int64_t world,
+                              double scale, int64_t max_ctas);
 
 // ---- ep_ops.cu
 void ep_scatter_rows(const at::Tensor& src, const at::Tensor& dst_rank, const at::Tensor& dst_row,
@@ -114,6 +118,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("dist_pack", &dmb::dist_pack);
   m.def("dist_apply", &dmb::dist_apply);
   m.def("dist_barrier", &dmb::dist_barrier);
+  m.def("fsdp_all_gather_pull", &dmb::fsdp_all_gather_pull);
+  m.def("fsdp_reduce_scatter_pull", &dmb::fsdp_reduce_scatter_pull);
   m.def("ep_scatter_rows", &dmb::ep_scatter_rows);
   m.def("ep_gather_rows", &dmb::ep_gather_rows);
   m.def("rope", &dmb::rope);

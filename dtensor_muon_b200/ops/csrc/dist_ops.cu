@@ -317,3 +317,72 @@ void dist_barrier(const at::Tensor& flag_base, int64_t rank, int64_t world, int6
 }
 
 }  // namespace dmb
+
+// ------------------------------------------------------------------------
+// FSDP collectives over peer memory (plugged into FSDP2 through its custom
+// all-gather / reduce-scatter hooks). Each rank's input is first staged in its
+// symmetric buffer; after a barrier every rank pulls what it needs.
+namespace dmb {
+namespace {
+
+// out[k * n + i] = staging_k[i] for every rank k (16-byte vectors).
+__global__ void ag_pull_kernel(uint4* __restrict__ out, const int64_t* peer_base, long long off, long long n_vec,
+                               int world) {
+  const long long total = n_vec * world;
+  for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (long long)gridDim.x * blockDim.x) {
+    const int k = (int)(i / n_vec);
+    const long long j = i - (long long)k * n_vec;
+    out[i] = reinterpret_cast<const uint4*>(peer_base[k] + off)[j];
+  }
+}
+
+// out[i] = scale * sum_k staging_k[rank * n + i], fp32 accumulation; dt 0 fp32 / 1 bf16.
+__global__ void rs_pull_kernel(void* __restrict__ out, const int64_t* peer_base, long long off, long long n, int rank,
+                               int world, int dt, float scale) {
+  const long long n8 = n / 8;
+  for (long long v = (long long)blockIdx.x * blockDim.x + threadIdx.x; v < n8; v += (long long)gridDim.x * blockDim.x) {
+    float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+    for (int k = 0; k < world; ++k) {
+      const void* src = reinterpret_cast<const void*>(peer_base[k] + off);
+      float x[8];
+      load8(src, dt, (long long)rank * n + v * 8, x);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) acc[e] += x[e];
+    }
+#pragma unroll
+    for (int e = 0; e < 8; ++e) acc[e] *= scale;
+    store8(out, dt, v * 8, acc);
+  }
+}
+
+}  // namespace
+
+void fsdp_all_gather_pull(at::Tensor& out, const at::Tensor& peer_base, int64_t off, int64_t in_bytes, int64_t world,
+                          int64_t max_ctas) {
+  const at::cuda::CUDAGuard guard(out.device());
+  TORCH_CHECK(in_bytes % 16 == 0 && off % 16 == 0 && out.is_contiguous());
+  TORCH_CHECK(out.numel() * out.element_size() == in_bytes * world);
+  const long long n_vec = in_bytes / 16;
+  if (n_vec == 0) return;
+  const int blocks = (int)std::min<long long>(max_ctas, (n_vec * world + 255) / 256);
+  ag_pull_kernel<<<blocks, 256, 0, at::cuda::getCurrentCUDAStream()>>>(reinterpret_cast<uint4*>(out.data_ptr()),
+                                                                       peer_base.data_ptr<int64_t>(), off, n_vec,
+                                                                       (int)world);
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+void fsdp_reduce_scatter_pull(at::Tensor& out, const at::Tensor& peer_base, int64_t off, int64_t rank, int64_t world,
+                              double scale, int64_t max_ctas) {
+  const at::cuda::CUDAGuard guard(out.device());
+  TORCH_CHECK(out.is_contiguous() && (out.scalar_type() == at::kFloat || out.scalar_type() == at::kBFloat16));
+  const long long n = out.numel();
+  TORCH_CHECK(n % 8 == 0 && off % 16 == 0);
+  if (n == 0) return;
+  const int blocks = (int)std::min<long long>(max_ctas, (n / 8 + 255) / 256);
+  rs_pull_kernel<<<blocks, 256, 0, at::cuda::getCurrentCUDAStream()>>>(
+      out.data_ptr(), peer_base.data_ptr<int64_t>(), off, n, (int)rank, (int)world,
+      out.scalar_type() == at::kFloat ? 0 : 1, (float)scale);
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+}  // namespace dmb

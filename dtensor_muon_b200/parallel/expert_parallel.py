@@ -142,7 +142,7 @@ class ExpertParallel:
 
     def _exchange(self, device) -> _P2PExchange:
         if self._p2p is None:
-            self._p2p = _P2PExchange(symm.workspace_for(self.group, device))
+            self._p2p = _P2PExchange(symm.workspace_for(self.group, device, "ep"))
         return self._p2p
 
     def plan(self, expert_ids: Tensor) -> tuple[_Plan, Tensor, Tensor]:

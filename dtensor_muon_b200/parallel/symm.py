@@ -86,11 +86,14 @@ class SymmetricWorkspace:
         _ext.check_device_errors(self.device)
 
 
-_WORKSPACES: dict[tuple[str, int], SymmetricWorkspace] = {}
+_WORKSPACES: dict[tuple[str, int, str], SymmetricWorkspace] = {}
 
 
-def workspace_for(group: dist.ProcessGroup, device: torch.device) -> SymmetricWorkspace:
-    key = (group.group_name, device.index if device.index is not None else torch.cuda.current_device())
+def workspace_for(group: dist.ProcessGroup, device: torch.device, purpose: str = "optim") -> SymmetricWorkspace:
+    """One workspace per (group, device, purpose): users that issue barriers on
+    different streams (optimizer, EP exchange, FSDP all-gather, FSDP
+    reduce-scatter) must not share a barrier epoch sequence."""
+    key = (group.group_name, device.index if device.index is not None else torch.cuda.current_device(), purpose)
     ws = _WORKSPACES.get(key)
     if ws is None:
         ws = SymmetricWorkspace(group, device)

@@ -27,6 +27,7 @@ def build_llama(
     seed: int | None = 0,
     block_factory=None,
     reshard_after_forward: bool = False,
+    fsdp_comm: str = "p2p",
 ) -> Llama:
     """Build a randomly initialised Llama on ``device`` without a host copy.
 
@@ -35,6 +36,9 @@ def build_llama(
     ``reshard_after_forward=False`` (default) keeps each block's gathered
     weights until its backward: with 180 GB of HBM per GPU the extra bf16 copy
     of an 8B model (16 GB) is cheap, and it removes the backward re-gather.
+    ``fsdp_comm="p2p"`` runs FSDP's all-gather / reduce-scatter on the NVLink
+    peer-memory kernels of :mod:`dtensor_muon_b200.parallel.fsdp_comm`;
+    ``"nccl"`` keeps FSDP2's NCCL collectives.
     """
     with torch.device("meta"):
         model = Llama(cfg, block_factory=block_factory).to(dtype)
@@ -44,6 +48,10 @@ def build_llama(
         for layer in model.layers:
             fully_shard(layer, mesh=mesh, reshard_after_forward=reshard_after_forward)
         fully_shard(model, mesh=mesh, reshard_after_forward=reshard_after_forward)
+        if fsdp_comm == "p2p" and mesh.size() > 1:
+            from .parallel.fsdp_comm import use_p2p_collectives
+
+            use_p2p_collectives(model)
     model.to_empty(device=device)
     if seed is not None:
         torch.manual_seed(seed + (dist.get_rank() if dist.is_initialized() else 0))

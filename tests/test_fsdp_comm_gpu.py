@@ -1,0 +1,47 @@
+"""FSDP2 with the P2P all-gather / reduce-scatter kernels against FSDP2 on NCCL (2 GPUs)."""
+
+import pytest
+import torch
+
+from testkit import run_distributed
+
+pytestmark = [pytest.mark.gpu, pytest.mark.multigpu]
+
+
+def _worker(rank, world):
+    import torch
+    from torch.distributed.device_mesh import init_device_mesh
+
+    from dtensor_muon_b200.models.llama import lm_loss, preset
+    from dtensor_muon_b200.ops import _ext
+    from dtensor_muon_b200.train import build_llama, build_optimizer
+
+    mesh = init_device_mesh("cuda", (world,))
+    cfg = preset("tiny", vocab_size=1024, dim=256, n_layers=2)
+    dev = torch.device("cuda", rank)
+    results = {}
+    for comm in ("nccl", "p2p"):
+        model = build_llama(cfg, dev, mesh=mesh, seed=0, fsdp_comm=comm)
+        opt = build_optimizer(model, lr=1e-2)
+        gen = torch.Generator().manual_seed(7 + rank)
+        losses = []
+        for _ in range(3):
+            ids = torch.randint(0, cfg.vocab_size, (2, 65), generator=gen).to(dev)
+            loss = lm_loss(model(ids[:, :-1]), ids[:, 1:])
+            loss.backward()
+            opt.step()
+            opt.zero_grad()
+            losses.append(loss.item())
+        results[comm] = (losses, [p.full_tensor().float() for p in model.parameters()])
+    torch.cuda.synchronize()
+    _ext.check_device_errors(dev)
+    for a, b in zip(results["nccl"][0], results["p2p"][0]):
+        assert abs(a - b) < 2e-2 * max(1.0, abs(a)), (a, b)
+    for x, y in zip(results["nccl"][1], results["p2p"][1]):
+        bad = (~torch.isclose(x, y, rtol=2e-2, atol=2e-2)).float().mean().item()
+        assert bad < 0.02, bad
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+def test_fsdp_p2p_collectives_match_nccl():
+    run_distributed(_worker, 2, backend="nccl", device_type="cuda")
