@@ -33,6 +33,8 @@ _LAUNCHES = {
     "dist_barrier": 1,
     "fsdp_all_gather_pull": 1,
     "fsdp_reduce_scatter_pull": 1,
+    "push_slots": 1,
+    "local_slot_sum": 1,
     "ep_scatter_rows": 1,
     "ep_gather_rows": 1,
     "rope": 1,

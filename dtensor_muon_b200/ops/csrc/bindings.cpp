@@ -55,6 +55,10 @@ void dist_apply(const at::Tensor& meta_i64, const at::Tensor& meta_i32, const at
 void dist_barrier(const at::Tensor& flag_base, int64_t rank, int64_t world, int64_t epoch);
 void fsdp_all_gather_pull(at::Tensor& out, const at::Tensor& peer_base, int64_t off, int64_t in_bytes, int64_t world,
                           int64_t max_ctas);
+void push_slots(const at::Tensor& src, const at::Tensor& peer_base, int64_t off, int64_t slot_bytes, int64_t rank,
+                int64_t world, bool per_peer, int64_t max_ctas);
+void local_slot_sum(at::Tensor& out, const at::Tensor& staging_bytes, int64_t off, int64_t world, double scale,
+                    int64_t max_ctas);
 void fsdp_reduce_scatter_pull(at::Tensor& out, const at::Tensor& peer_base, int64_t off, int64_t rank, int64_t world,
                               double scale, int64_t max_ctas);
 
@@ -120,6 +124,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("dist_barrier", &dmb::dist_barrier);
   m.def("fsdp_all_gather_pull", &dmb::fsdp_all_gather_pull);
   m.def("fsdp_reduce_scatter_pull", &dmb::fsdp_reduce_scatter_pull);
+  m.def("push_slots", &dmb::push_slots);
+  m.def("local_slot_sum", &dmb::local_slot_sum);
   m.def("ep_scatter_rows", &dmb::ep_scatter_rows);
   m.def("ep_gather_rows", &dmb::ep_gather_rows);
   m.def("rope", &dmb::rope);

@@ -325,29 +325,64 @@ void dist_barrier(const at::Tensor& flag_base, int64_t rank, int64_t world, int6
 namespace dmb {
 namespace {
 
-// out[k * n + i] = staging_k[i] for every rank k (16-byte vectors).
+// out[k * n + i] = staging_k[i] for every rank k (16-byte vectors). Each
+// thread keeps UNROLL independent loads in flight to cover NVLink latency.
+constexpr int AG_UNROLL = 4;
 __global__ void ag_pull_kernel(uint4* __restrict__ out, const int64_t* peer_base, long long off, long long n_vec,
                                int world) {
   const long long total = n_vec * world;
-  for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (long long)gridDim.x * blockDim.x) {
-    const int k = (int)(i / n_vec);
-    const long long j = i - (long long)k * n_vec;
-    out[i] = reinterpret_cast<const uint4*>(peer_base[k] + off)[j];
+  const long long stride = (long long)gridDim.x * blockDim.x;
+  for (long long i0 = (long long)blockIdx.x * blockDim.x + threadIdx.x; i0 < total; i0 += stride * AG_UNROLL) {
+    uint4 v[AG_UNROLL];
+#pragma unroll
+    for (int u = 0; u < AG_UNROLL; ++u) {
+      const long long i = i0 + u * stride;
+      if (i < total) {
+        const int k = (int)(i / n_vec);
+        v[u] = reinterpret_cast<const uint4*>(peer_base[k] + off)[i - (long long)k * n_vec];
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < AG_UNROLL; ++u) {
+      const long long i = i0 + u * stride;
+      if (i < total) out[i] = v[u];
+    }
   }
 }
 
 // out[i] = scale * sum_k staging_k[rank * n + i], fp32 accumulation; dt 0 fp32 / 1 bf16.
+// All peers' loads for a vector are issued before any is consumed.
+constexpr int RS_MAX_WORLD = 8;
 __global__ void rs_pull_kernel(void* __restrict__ out, const int64_t* peer_base, long long off, long long n, int rank,
                                int world, int dt, float scale) {
   const long long n8 = n / 8;
   for (long long v = (long long)blockIdx.x * blockDim.x + threadIdx.x; v < n8; v += (long long)gridDim.x * blockDim.x) {
     float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-    for (int k = 0; k < world; ++k) {
-      const void* src = reinterpret_cast<const void*>(peer_base[k] + off);
-      float x[8];
-      load8(src, dt, (long long)rank * n + v * 8, x);
+    const long long idx = (long long)rank * n + v * 8;
+    if (dt == 1 && world <= RS_MAX_WORLD) {
+      uint4 raw[RS_MAX_WORLD];
 #pragma unroll
-      for (int e = 0; e < 8; ++e) acc[e] += x[e];
+      for (int k = 0; k < RS_MAX_WORLD; ++k)
+        if (k < world)
+          raw[k] = *reinterpret_cast<const uint4*>(reinterpret_cast<const __nv_bfloat16*>(peer_base[k] + off) + idx);
+#pragma unroll
+      for (int k = 0; k < RS_MAX_WORLD; ++k) {
+        if (k < world) {
+          const uint32_t w[4] = {raw[k].x, raw[k].y, raw[k].z, raw[k].w};
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            acc[2 * e] += bf16_bits_to_float((uint16_t)(w[e] & 0xFFFFu));
+            acc[2 * e + 1] += bf16_bits_to_float((uint16_t)(w[e] >> 16));
+          }
+        }
+      }
+    } else {
+      for (int k = 0; k < world; ++k) {
+        float x[8];
+        load8(reinterpret_cast<const void*>(peer_base[k] + off), dt, idx, x);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) acc[e] += x[e];
+      }
     }
 #pragma unroll
     for (int e = 0; e < 8; ++e) acc[e] *= scale;
@@ -381,6 +416,80 @@ void fsdp_reduce_scatter_pull(at::Tensor& out, const at::Tensor& peer_base, int6
   const int blocks = (int)std::min<long long>(max_ctas, (n / 8 + 255) / 256);
   rs_pull_kernel<<<blocks, 256, 0, at::cuda::getCurrentCUDAStream()>>>(
       out.data_ptr(), peer_base.data_ptr<int64_t>(), off, n, (int)rank, (int)world,
+      out.scalar_type() == at::kFloat ? 0 : 1, (float)scale);
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+}  // namespace dmb
+
+// ---- push variants: stores into peers' staging (one barrier per collective)
+namespace dmb {
+namespace {
+
+// For every rank k: peer_k[off + rank * slot_bytes + i] = src[(per_peer ? k * slot_bytes : 0) + i].
+// grid.y walks the peers (rotated by rank so ranks spread over peers); each
+// thread keeps 4 independent 16-byte stores in flight; no division in the loop.
+__global__ void push_slots_kernel(const uint4* __restrict__ src, const int64_t* peer_base, long long off,
+                                  long long slot_vec, int rank, int world, int per_peer) {
+  const int k = (blockIdx.y + rank) % world;
+  uint4* dst = reinterpret_cast<uint4*>(peer_base[k] + off) + (long long)rank * slot_vec;
+  const uint4* s = src + (per_peer ? (long long)k * slot_vec : 0);
+  const long long stride = (long long)gridDim.x * blockDim.x;
+  long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+  for (; i + 3 * stride < slot_vec; i += 4 * stride) {
+    const uint4 a = s[i], b = s[i + stride], c = s[i + 2 * stride], d = s[i + 3 * stride];
+    dst[i] = a;
+    dst[i + stride] = b;
+    dst[i + 2 * stride] = c;
+    dst[i + 3 * stride] = d;
+  }
+  for (; i < slot_vec; i += stride) dst[i] = s[i];
+}
+
+// out[i] = scale * sum_j staging[j * n + i] (local), dt 0 fp32 / 1 bf16.
+__global__ void local_slot_sum_kernel(void* __restrict__ out, const void* __restrict__ staging, long long n, int world,
+                                      int dt, float scale) {
+  const long long n8 = n / 8;
+  for (long long v = (long long)blockIdx.x * blockDim.x + threadIdx.x; v < n8; v += (long long)gridDim.x * blockDim.x) {
+    float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+    for (int j = 0; j < world; ++j) {
+      float x[8];
+      load8(staging, dt, (long long)j * n + v * 8, x);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) acc[e] += x[e];
+    }
+#pragma unroll
+    for (int e = 0; e < 8; ++e) acc[e] *= scale;
+    store8(out, dt, v * 8, acc);
+  }
+}
+
+}  // namespace
+
+void push_slots(const at::Tensor& src, const at::Tensor& peer_base, int64_t off, int64_t slot_bytes, int64_t rank,
+                int64_t world, bool per_peer, int64_t max_ctas) {
+  const at::cuda::CUDAGuard guard(src.device());
+  TORCH_CHECK(src.is_contiguous() && slot_bytes % 16 == 0 && off % 16 == 0);
+  TORCH_CHECK(src.numel() * src.element_size() == (per_peer ? slot_bytes * world : slot_bytes));
+  const long long slot_vec = slot_bytes / 16;
+  if (slot_vec == 0) return;
+  const int per = (int)std::max<long long>(1, std::min<long long>(max_ctas / world, (slot_vec + 1023) / 1024));
+  push_slots_kernel<<<dim3(per, (unsigned)world), 256, 0, at::cuda::getCurrentCUDAStream()>>>(
+      reinterpret_cast<const uint4*>(src.data_ptr()), peer_base.data_ptr<int64_t>(), off, slot_vec, (int)rank,
+      (int)world, per_peer ? 1 : 0);
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+void local_slot_sum(at::Tensor& out, const at::Tensor& staging_bytes, int64_t off, int64_t world, double scale,
+                    int64_t max_ctas) {
+  const at::cuda::CUDAGuard guard(out.device());
+  TORCH_CHECK(out.is_contiguous() && (out.scalar_type() == at::kFloat || out.scalar_type() == at::kBFloat16));
+  const long long n = out.numel();
+  TORCH_CHECK(n % 8 == 0 && off % 16 == 0);
+  if (n == 0) return;
+  const int blocks = (int)std::min<long long>(max_ctas, (n / 8 + 255) / 256);
+  local_slot_sum_kernel<<<blocks, 256, 0, at::cuda::getCurrentCUDAStream()>>>(
+      out.data_ptr(), static_cast<const char*>(staging_bytes.data_ptr()) + off, n, (int)world,
       out.scalar_type() == at::kFloat ? 0 : 1, (float)scale);
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
