@@ -43,12 +43,6 @@ class SymmetricWorkspace:
         self.rank = dist.get_rank(group)
         self.world = dist.get_world_size(group)
         name = group.group_name
-        enable = getattr(symm_mem, "enable_symm_mem_for_group", None)
-        if enable is not None:
-            try:
-                enable(name)
-            except Exception:  # already enabled / not needed on this version
-                pass
         self._flags = symm_mem.empty(max(64, self.world), dtype=torch.int32, device=device)
         self._flags.zero_()
         hdl = symm_mem.rendezvous(self._flags, name)

@@ -1,0 +1,30 @@
+"""Config 1: 20-step CPU fp32 training parity with the unmodified reference optimizer."""
+
+import json
+import os
+import subprocess
+import sys
+
+import pytest
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+REF = os.path.join(ROOT, "baseline", "_ref", "muonium")
+
+
+def _run(impl):
+    env = dict(os.environ, TORCH_COMPILE_DISABLE="1", CUDA_VISIBLE_DEVICES="")
+    out = subprocess.run(
+        [sys.executable, "-m", "dtensor_muon_b200.testing.parity", "--impl", impl],
+        cwd=ROOT, env=env, capture_output=True, text=True, timeout=600,
+    )
+    assert out.returncode == 0, out.stderr[-2000:]
+    return json.loads(out.stdout.strip().splitlines()[-1])
+
+
+@pytest.mark.skipif(not os.path.isdir(REF), reason="reference not installed under baseline/_ref")
+def test_losses_and_params_match_reference_cpu():
+    ours, ref = _run("ours"), _run("reference")
+    assert len(ours["losses"]) == len(ref["losses"]) == 20
+    for a, b in zip(ours["losses"], ref["losses"]):
+        assert abs(a - b) <= 1e-4 * max(1.0, abs(b)), (a, b)
+    assert abs(ours["param_abs_sum"] - ref["param_abs_sum"]) <= 1e-5 * ref["param_abs_sum"]
