@@ -19,6 +19,8 @@ _LAUNCHES = {
     "gram_sym2": 1,
     "gemm_ax2": 1,
     "muon_pack": 1,
+    "muon_pack_ex": 1,
+    "muon_apply_ex": 1,
     "norm_finalize": 1,
     "muon_apply": 1,
     "muon_unpack": 1,

@@ -28,6 +28,12 @@ int64_t get_gemm_variant();
 at::Tensor muon_pack(const at::Tensor& src_ptrs, const c10::optional<at::Tensor>& buf_ptrs, int64_t src_dtype_code,
                      int64_t R, int64_t C, int64_t ld, bool transpose, at::Tensor& out, double momentum,
                      bool nesterov, bool maximize);
+at::Tensor muon_pack_ex(const at::Tensor& src_ptrs, const c10::optional<at::Tensor>& buf_ptrs, int64_t src_dtype_code,
+                        int64_t R, int64_t C, int64_t ld, bool transpose, at::Tensor& out, double momentum,
+                        bool nesterov, bool maximize, bool vec_ok);
+void muon_apply_ex(const at::Tensor& ws, bool transpose, int64_t R, int64_t C, int64_t ld, const at::Tensor& dst_ptrs,
+                   int64_t dst_dtype_code, const c10::optional<at::Tensor>& rowscale,
+                   const c10::optional<at::Tensor>& mat_scale, double lr_eff, double wd, bool cautious, bool vec_ok);
 at::Tensor norm_finalize(const at::Tensor& partial, double fac, double eps);
 void muon_apply(const at::Tensor& ws, bool transpose, int64_t R, int64_t C, int64_t ld, const at::Tensor& dst_ptrs,
                 int64_t dst_dtype_code, const c10::optional<at::Tensor>& rowscale,
@@ -110,6 +116,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("set_gemm_variant", &dmb::set_gemm_variant);
   m.def("get_gemm_variant", &dmb::get_gemm_variant);
   m.def("muon_pack", &dmb::muon_pack);
+  m.def("muon_pack_ex", &dmb::muon_pack_ex);
+  m.def("muon_apply_ex", &dmb::muon_apply_ex);
   m.def("norm_finalize", &dmb::norm_finalize);
   m.def("muon_apply", &dmb::muon_apply);
   m.def("muon_unpack", &dmb::muon_unpack);

@@ -65,6 +65,7 @@ struct DistArgs {
   int tiles_c;
   float lr_eff, wd;
   int cautious, has_rowscale;
+  int vec_ok;           // host checked: every local pointer is 16-byte aligned
 };
 
 __device__ __forceinline__ float block_sum(float v, float* red) {
@@ -198,6 +199,167 @@ __global__ void __launch_bounds__(NT) dist_apply_rows_kernel(const DistArgs a) {
   }
 }
 
+
+// ---- vectorised owner-compute kernels (C % 8 == 0, row chunk % 8 == 0) -----
+__device__ __forceinline__ void dist_momentum8(const DistArgs& a, const void* g, float* buf, long long idx,
+                                               float (&v)[8]) {
+  load8(g, a.grad_dtype, idx, v);
+  if (a.maximize)
+#pragma unroll
+    for (int k = 0; k < 8; ++k) v[k] = -v[k];
+  if (buf) {
+    float m[8];
+    load8(buf, 0, idx, m);
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      m[k] = fmaf(m[k], a.momentum, v[k]);
+      v[k] = a.nesterov ? fmaf(m[k], a.momentum, v[k]) : m[k];
+    }
+    store8(buf, 0, idx, m);
+  }
+#pragma unroll
+  for (int k = 0; k < 8; ++k) v[k] = __bfloat162float(__float2bfloat16_rn(v[k]));
+}
+
+// Non-transposed: rows [r0, g1) x cols [0, Mp): 16 rows x 128 cols per CTA.
+__global__ void __launch_bounds__(NT) dist_pack_rows_vec(const DistArgs a) {
+  __shared__ float red[NT / 32];
+  const int b = blockIdx.y;
+  const int tr = blockIdx.x / a.tiles_c, tc = blockIdx.x % a.tiles_c;
+  const int gr = a.r0 + tr * 16 + (threadIdx.x >> 4), c = tc * 128 + (threadIdx.x & 15) * 8;
+  float v[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+  float ss = 0.f;
+  if (gr < a.r1 && c < a.C) {
+    const long long idx = (long long)(gr - a.r0) * a.C + c;
+    dist_momentum8(a, reinterpret_cast<const void*>(a.grad[b]), a.buf ? reinterpret_cast<float*>(a.buf[b]) : nullptr,
+                   idx, v);
+#pragma unroll
+    for (int k = 0; k < 8; ++k) ss = fmaf(v[k], v[k], ss);
+  }
+  if (gr < a.g1 && c < a.Mp) {
+    __nv_bfloat16* X = reinterpret_cast<__nv_bfloat16*>(a.peer_base[a.owner[b]] + a.x_off) +
+                       (long long)a.slot[b] * a.Np * a.Mp;
+    store8(X, 1, (long long)gr * a.Mp + c, v);
+  }
+  const float tot = block_sum(ss, red);
+  if (threadIdx.x == 0) a.partial[(long long)b * gridDim.x + blockIdx.x] = tot;
+}
+
+// Transposed: 64 local rows x 64 cols through shared memory; X[c][gr .. gr+7] stored as 16 bytes.
+__global__ void __launch_bounds__(NT) dist_pack_tr_vec(const DistArgs a) {
+  __shared__ float tile[T][T + 1];
+  __shared__ float red[NT / 32];
+  const int b = blockIdx.y;
+  const int tr = blockIdx.x / a.tiles_c, tc = blockIdx.x % a.tiles_c;
+  const int g0 = a.r0 + tr * T, c0 = tc * T;
+  const int lane8 = (threadIdx.x & 7) * 8, row = threadIdx.x >> 3;
+  const void* g = reinterpret_cast<const void*>(a.grad[b]);
+  float* buf = a.buf ? reinterpret_cast<float*>(a.buf[b]) : nullptr;
+  float ss = 0.f;
+#pragma unroll
+  for (int it = 0; it < 2; ++it) {
+    const int i = row + it * 32;
+    const int gr = g0 + i, c = c0 + lane8;
+    float v[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+    if (gr < a.r1 && c < a.C) {
+      dist_momentum8(a, g, buf, (long long)(gr - a.r0) * a.C + c, v);
+#pragma unroll
+      for (int k = 0; k < 8; ++k) ss = fmaf(v[k], v[k], ss);
+    }
+#pragma unroll
+    for (int k = 0; k < 8; ++k) tile[i][lane8 + k] = v[k];
+  }
+  __syncthreads();
+  __nv_bfloat16* X = reinterpret_cast<__nv_bfloat16*>(a.peer_base[a.owner[b]] + a.x_off) +
+                     (long long)a.slot[b] * a.Np * a.Mp;
+#pragma unroll
+  for (int it = 0; it < 2; ++it) {
+    const int j = row + it * 32;  // column offset within the tile
+    const int c = c0 + j, gr = g0 + lane8;
+    if (c < a.Np && gr < a.g1) {
+      float v[8];
+#pragma unroll
+      for (int k = 0; k < 8; ++k) v[k] = tile[lane8 + k][j];
+      store8(X, 1, (long long)c * a.Mp + gr, v);
+    }
+  }
+  const float tot = block_sum(ss, red);
+  if (threadIdx.x == 0) a.partial[(long long)b * gridDim.x + blockIdx.x] = tot;
+}
+
+__device__ __forceinline__ void dist_apply8(const DistArgs& a, int b, int gr, int c, float (&u)[8], const float* rs) {
+  if (rs) {
+    const float f = rs[gr];
+#pragma unroll
+    for (int k = 0; k < 8; ++k) u[k] *= f;
+  }
+  void* P = reinterpret_cast<void*>(a.param[b]);
+  const long long idx = (long long)(gr - a.r0) * a.C + c;
+  float p[8];
+  load8(P, a.param_dtype, idx, p);
+#pragma unroll
+  for (int k = 0; k < 8; ++k) {
+    float x = u[k];
+    if (a.wd != 0.f && (!a.cautious || x * p[k] > 0.f)) x = fmaf(a.wd, p[k], x);
+    p[k] = fmaf(-a.lr_eff, x, p[k]);
+  }
+  store8(P, a.param_dtype, idx, p);
+}
+
+__global__ void __launch_bounds__(NT) dist_apply_rows_vec(const DistArgs a) {
+  const int b = blockIdx.y;
+  const int tr = blockIdx.x / a.tiles_c, tc = blockIdx.x % a.tiles_c;
+  const int gr = a.r0 + tr * 16 + (threadIdx.x >> 4), c = tc * 128 + (threadIdx.x & 15) * 8;
+  const int64_t base = a.peer_base[a.owner[b]];
+  if (a.var && tc == 0 && (threadIdx.x & 15) == 0 && gr < a.r1) {
+    const float* vsrc = reinterpret_cast<const float*>(base + a.vbuf_off) + (long long)a.slot[b] * a.R;
+    reinterpret_cast<float*>(a.var[b])[gr - a.r0] = vsrc[gr];
+  }
+  if (gr >= a.r1 || c >= a.C) return;
+  const __nv_bfloat16* U = reinterpret_cast<const __nv_bfloat16*>(base + a.res_off) + (long long)a.slot[b] * a.Np * a.Mp;
+  const float* rs = a.has_rowscale ? reinterpret_cast<const float*>(base + a.rs_off) + (long long)a.slot[b] * a.R : nullptr;
+  float u[8];
+  load8(U, 1, (long long)gr * a.Mp + c, u);
+  dist_apply8(a, b, gr, c, u, rs);
+}
+
+__global__ void __launch_bounds__(NT) dist_apply_tr_vec(const DistArgs a) {
+  __shared__ float tile[T][T + 1];
+  const int b = blockIdx.y;
+  const int tr = blockIdx.x / a.tiles_c, tc = blockIdx.x % a.tiles_c;
+  const int g0 = a.r0 + tr * T, c0 = tc * T;
+  const int64_t base = a.peer_base[a.owner[b]];
+  const __nv_bfloat16* U = reinterpret_cast<const __nv_bfloat16*>(base + a.res_off) + (long long)a.slot[b] * a.Np * a.Mp;
+  const float* rs = a.has_rowscale ? reinterpret_cast<const float*>(base + a.rs_off) + (long long)a.slot[b] * a.R : nullptr;
+  const int lane8 = (threadIdx.x & 7) * 8, row = threadIdx.x >> 3;
+#pragma unroll
+  for (int it = 0; it < 2; ++it) {
+    const int j = row + it * 32;  // workspace row = param column c0 + j
+    float v[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+    if (c0 + j < a.C && g0 + lane8 < a.r1) load8(U, 1, (long long)(c0 + j) * a.Mp + g0 + lane8, v);
+#pragma unroll
+    for (int k = 0; k < 8; ++k) tile[j][lane8 + k] = v[k];
+  }
+  __syncthreads();
+#pragma unroll
+  for (int it = 0; it < 2; ++it) {
+    const int i = row + it * 32;
+    const int gr = g0 + i, c = c0 + lane8;
+    if (gr >= a.r1 || c >= a.C) continue;
+    float u[8];
+#pragma unroll
+    for (int k = 0; k < 8; ++k) u[k] = tile[lane8 + k][i];
+    dist_apply8(a, b, gr, c, u, rs);
+  }
+  if (a.var && tc == 0) {
+    const float* vsrc = reinterpret_cast<const float*>(base + a.vbuf_off) + (long long)a.slot[b] * a.R;
+    for (int i = threadIdx.x; i < T; i += NT) {
+      const int gr = g0 + i;
+      if (gr < a.r1) reinterpret_cast<float*>(a.var[b])[gr - a.r0] = vsrc[gr];
+    }
+  }
+}
+
 // flags: uint32 [world] at offset 0 of every rank's flag buffer. Rank r
 // announces epoch e by writing flags[r] = e on every peer, then waits until
 // its own flags[k] >= e for all k. Bounded: gives up after kWaitTimeoutNs.
@@ -264,6 +426,7 @@ DistArgs make_args(const at::Tensor& meta_i64, const at::Tensor& meta_i32, const
   a.maximize = ints[18];
   a.cautious = ints[19];
   a.has_rowscale = ints[20];
+  a.vec_ok = ints.size() > 21 ? (int)ints[21] : 0;
   a.momentum = floats[0];
   a.lr_eff = floats[1];
   a.wd = floats[2];
@@ -283,14 +446,25 @@ void dist_pack(const at::Tensor& meta_i64, const at::Tensor& meta_i32, const at:
   const int rows = a.g1 - a.r0;
   const int tiles_r = rows > 0 ? (rows + T - 1) / T : 0;
   const int nblk = tiles_r * a.tiles_c;
-  auto partial = at::zeros({B, std::max(nblk, 1)}, meta_i64.options().dtype(at::kFloat));
-  a.partial = partial.data_ptr<float>();
   auto st = at::cuda::getCurrentCUDAStream();
-  if (nblk > 0) {
-    dist_pack_rows_kernel<<<dim3(nblk, B), NT, 0, st>>>(a);
+  const bool vec = a.vec_ok && (a.C % 8 == 0) && (a.r0 % 8 == 0) && (a.r1 % 8 == 0 || a.r1 == a.R) && (a.R % 8 == 0);
+  int grid_x = nblk;
+  if (vec && !a.transpose) {
+    a.tiles_c = a.Mp / 128;
+    grid_x = rows > 0 ? ((rows + 15) / 16) * a.tiles_c : 0;
+  }
+  auto partial = at::zeros({B, std::max(grid_x, 1)}, meta_i64.options().dtype(at::kFloat));
+  a.partial = partial.data_ptr<float>();
+  if (grid_x > 0) {
+    if (vec && !a.transpose)
+      dist_pack_rows_vec<<<dim3(grid_x, B), NT, 0, st>>>(a);
+    else if (vec)
+      dist_pack_tr_vec<<<dim3(grid_x, B), NT, 0, st>>>(a);
+    else
+      dist_pack_rows_kernel<<<dim3(grid_x, B), NT, 0, st>>>(a);
     C10_CUDA_KERNEL_LAUNCH_CHECK();
   }
-  dist_push_sums_kernel<<<B, NT, 0, st>>>(a, std::max(nblk, 1));
+  dist_push_sums_kernel<<<B, NT, 0, st>>>(a, std::max(grid_x, 1));
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 
@@ -303,8 +477,17 @@ void dist_apply(const at::Tensor& meta_i64, const at::Tensor& meta_i32, const at
   a.tiles_c = (a.C + T - 1) / T;
   const int rows = a.r1 - a.r0;
   if (rows <= 0) return;
-  const int tiles_r = (rows + T - 1) / T;
-  dist_apply_rows_kernel<<<dim3(tiles_r * a.tiles_c, B), NT, 0, at::cuda::getCurrentCUDAStream()>>>(a);
+  auto st = at::cuda::getCurrentCUDAStream();
+  const bool vec = a.vec_ok && (a.C % 8 == 0) && (a.r0 % 8 == 0) && (a.r1 % 8 == 0 || a.r1 == a.R) && (a.R % 8 == 0);
+  if (vec && !a.transpose) {
+    a.tiles_c = (a.C + 127) / 128;
+    dist_apply_rows_vec<<<dim3(((rows + 15) / 16) * a.tiles_c, B), NT, 0, st>>>(a);
+  } else if (vec) {
+    dist_apply_tr_vec<<<dim3(((rows + T - 1) / T) * a.tiles_c, B), NT, 0, st>>>(a);
+  } else {
+    const int tiles_r = (rows + T - 1) / T;
+    dist_apply_rows_kernel<<<dim3(tiles_r * a.tiles_c, B), NT, 0, st>>>(a);
+  }
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 

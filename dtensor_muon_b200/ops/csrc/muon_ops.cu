@@ -431,9 +431,9 @@ __global__ void __launch_bounds__(256) normuon_finalize_kernel(const float* rows
 
 // Packs B matrices (pointers in `src`, optional fp32 momentum `buf`) into the
 // bf16 workspace `out` [B, Np, Mp]; returns per-tile partial sums of squares.
-at::Tensor muon_pack(const at::Tensor& src_ptrs, const c10::optional<at::Tensor>& buf_ptrs, int64_t src_dtype_code,
-                     int64_t R, int64_t C, int64_t ld, bool transpose, at::Tensor& out, double momentum,
-                     bool nesterov, bool maximize) {
+at::Tensor muon_pack_ex(const at::Tensor& src_ptrs, const c10::optional<at::Tensor>& buf_ptrs, int64_t src_dtype_code,
+                        int64_t R, int64_t C, int64_t ld, bool transpose, at::Tensor& out, double momentum,
+                        bool nesterov, bool maximize, bool vec_ok) {
   TORCH_CHECK(out.is_cuda() && out.dim() == 3 && out.scalar_type() == at::kBFloat16 && out.is_contiguous());
   const int B = out.size(0), Np = out.size(1), Mp = out.size(2);
   TORCH_CHECK(Np % TILE == 0 && Mp % TILE == 0);
@@ -460,7 +460,7 @@ at::Tensor muon_pack(const at::Tensor& src_ptrs, const c10::optional<at::Tensor>
   a.partial = partial.data_ptr<float>();
   a.tiles_c = tiles_c;
   auto st = at::cuda::getCurrentCUDAStream();
-  if (C % 8 == 0 && ld % 8 == 0) {
+  if (vec_ok && C % 8 == 0 && ld % 8 == 0) {
     if (!transpose) {
       a.tiles_c = Mp / 128;
       auto p2 = at::empty({B, (Np / 16) * a.tiles_c}, out.options().dtype(at::kFloat));
@@ -479,6 +479,14 @@ at::Tensor muon_pack(const at::Tensor& src_ptrs, const c10::optional<at::Tensor>
   return partial;
 }
 
+// Plain entry points: every matrix pointer is assumed 16-byte aligned (torch allocations).
+at::Tensor muon_pack(const at::Tensor& src_ptrs, const c10::optional<at::Tensor>& buf_ptrs, int64_t src_dtype_code,
+                     int64_t R, int64_t C, int64_t ld, bool transpose, at::Tensor& out, double momentum,
+                     bool nesterov, bool maximize) {
+  return muon_pack_ex(src_ptrs, buf_ptrs, src_dtype_code, R, C, ld, transpose, out, momentum, nesterov, maximize,
+                      true);
+}
+
 // partial [B, P] -> inv_norm [B] = 1 / (sqrt(sum) * fac + eps)
 at::Tensor norm_finalize(const at::Tensor& partial, double fac, double eps) {
   const at::cuda::CUDAGuard guard(partial.device());
@@ -490,9 +498,9 @@ at::Tensor norm_finalize(const at::Tensor& partial, double fac, double eps) {
   return inv;
 }
 
-void muon_apply(const at::Tensor& ws, bool transpose, int64_t R, int64_t C, int64_t ld, const at::Tensor& dst_ptrs,
-                int64_t dst_dtype_code, const c10::optional<at::Tensor>& rowscale,
-                const c10::optional<at::Tensor>& mat_scale, double lr_eff, double wd, bool cautious) {
+void muon_apply_ex(const at::Tensor& ws, bool transpose, int64_t R, int64_t C, int64_t ld, const at::Tensor& dst_ptrs,
+                   int64_t dst_dtype_code, const c10::optional<at::Tensor>& rowscale,
+                   const c10::optional<at::Tensor>& mat_scale, double lr_eff, double wd, bool cautious, bool vec_ok) {
   const at::cuda::CUDAGuard guard(ws.device());
   const int B = ws.size(0);
   ApplyArgs a{};
@@ -512,7 +520,7 @@ void muon_apply(const at::Tensor& ws, bool transpose, int64_t R, int64_t C, int6
   a.cautious = cautious;
   a.mode = 0;
   auto st = at::cuda::getCurrentCUDAStream();
-  if (C % 8 == 0 && ld % 8 == 0) {
+  if (vec_ok && C % 8 == 0 && ld % 8 == 0) {
     if (!transpose) {
       a.tiles_c = (C + 127) / 128;
       muon_apply_rows_vec<<<dim3(((R + 15) / 16) * a.tiles_c, B), PACK_THREADS, 0, st>>>(a);
@@ -527,6 +535,12 @@ void muon_apply(const at::Tensor& ws, bool transpose, int64_t R, int64_t C, int6
   dim3 grid(((R + TILE - 1) / TILE) * a.tiles_c, B);
   muon_apply_kernel<<<grid, PACK_THREADS, 0, st>>>(a);
   C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+void muon_apply(const at::Tensor& ws, bool transpose, int64_t R, int64_t C, int64_t ld, const at::Tensor& dst_ptrs,
+                int64_t dst_dtype_code, const c10::optional<at::Tensor>& rowscale,
+                const c10::optional<at::Tensor>& mat_scale, double lr_eff, double wd, bool cautious) {
+  muon_apply_ex(ws, transpose, R, C, ld, dst_ptrs, dst_dtype_code, rowscale, mat_scale, lr_eff, wd, cautious, true);
 }
 
 // Workspace -> contiguous bf16 [B, R, C] (undoing the transpose), optionally

@@ -117,11 +117,16 @@ def fused_muon_update(
             x = WORKSPACE.get(device, "x", (B, lay.Np, lay.Mp))
             packed = ptr_tensor([e[1] for e in part] + [e[2] for e in part] + [e[0] for e in part], device)
             gptrs, bptrs, pptrs = packed[:B], packed[B : 2 * B], packed[2 * B :]
+            # 16-byte vector I/O only when every matrix pointer is aligned
+            # (views into sharded / flat storage need not be).
+            vec_ok = all(e[i] % 16 == 0 for e in part for i in range(3))
             if momentum_done:
-                partial = C_.muon_pack(gptrs, None, dtype_code(gdt), R, C, C, lay.transpose, x, 0.0, False, False)
+                partial = C_.muon_pack_ex(
+                    gptrs, None, dtype_code(gdt), R, C, C, lay.transpose, x, 0.0, False, False, vec_ok
+                )
             else:
-                partial = C_.muon_pack(
-                    gptrs, bptrs, dtype_code(gdt), R, C, C, lay.transpose, x, momentum, nesterov, maximize
+                partial = C_.muon_pack_ex(
+                    gptrs, bptrs, dtype_code(gdt), R, C, C, lay.transpose, x, momentum, nesterov, maximize, vec_ok
                 )
             inv = C_.norm_finalize(partial, fac, eps)
             res = run_iteration(x, inv, lay, ns_steps, strategy)
@@ -133,7 +138,7 @@ def fused_muon_update(
                     rowsq.mul_(mat_scale.view(-1, 1).square())
                 vptrs = ptr_tensor([e[3] for e in part], device)
                 rowscale = C_.normuon_finalize(rowsq, vptrs, C, muon_beta2)
-            C_.muon_apply(
+            C_.muon_apply_ex(
                 res,
                 lay.transpose,
                 R,
@@ -146,4 +151,5 @@ def fused_muon_update(
                 lr_eff,
                 float(weight_decay),
                 bool(cautious_wd),
+                vec_ok,
             )

@@ -156,7 +156,10 @@ def orthogonalize_native(
         B = len(part)
         x = WORKSPACE.get(device, "x", (B, lay.Np, lay.Mp))
         ptrs = ptr_tensor([m.data_ptr() for m in part], device)
-        partial = C.muon_pack(ptrs, None, dtype_code(part[0].dtype), R, Cc, Cc, lay.transpose, x, 0.0, False, False)
+        vec_ok = all(m.data_ptr() % 16 == 0 for m in part)
+        partial = C.muon_pack_ex(
+            ptrs, None, dtype_code(part[0].dtype), R, Cc, Cc, lay.transpose, x, 0.0, False, False, vec_ok
+        )
         inv = C.norm_finalize(partial, norm_factor(strategy), eps)
         if steps == 0:
             out = C.muon_unpack(x, lay.transpose, R, Cc, inv)

@@ -144,6 +144,7 @@ def _run_batch(C_, ws, sel, params, grads, buffers, variances, lr_eff, lay, R, C
         dtype_code(grads[sel[0]].dtype), dtype_code(params[sel[0]].dtype),
         R, C, int(lay.transpose), lay.Np, lay.Mp, r0, r1, g1, rank, world,
         int(nesterov), int(maximize), int(cautious_wd), int(has_var),
+        int(all(x % 16 == 0 for row in ptrs[:3] for x in row)),
     ]
     floats = [float(momentum), float(lr_eff), float(weight_decay)]
 

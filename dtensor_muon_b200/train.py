@@ -48,6 +48,12 @@ def build_llama(
         for layer in model.layers:
             fully_shard(layer, mesh=mesh, reshard_after_forward=reshard_after_forward)
         fully_shard(model, mesh=mesh, reshard_after_forward=reshard_after_forward)
+        # Issue each block's parameter all-gather two blocks ahead of its forward.
+        layers = list(model.layers)
+        for i, layer in enumerate(layers):
+            nxt = layers[i + 1 : i + 3]
+            if nxt:
+                layer.set_modules_to_forward_prefetch(nxt)
         if fsdp_comm == "p2p" and mesh.size() > 1:
             from .parallel.fsdp_comm import use_p2p_collectives
 
