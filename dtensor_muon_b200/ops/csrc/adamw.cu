@@ -39,7 +39,8 @@ __device__ __forceinline__ void st(void* p, int dt, long long i, float v) {
     reinterpret_cast<__nv_bfloat16*>(p)[i] = __float2bfloat16_rn(v);
 }
 
-__global__ void __launch_bounds__(ADAM_THREADS) adamw_kernel(const AdamArgs a) {
+// (256 threads, >= 4 CTAs per SM: caps registers so enough loads are in flight)
+__global__ void __launch_bounds__(ADAM_THREADS, 4) adamw_kernel(const AdamArgs a) {
   // Find the tensor this CTA works on (meta[t][7] = first block index, ascending).
   int lo = 0, hi = a.ntensors - 1;
   const int blk = blockIdx.x;
