@@ -22,6 +22,7 @@ import torch
 from torch import Tensor
 from torch.distributed.tensor import DTensor
 
+from ..utils.tracing import nvtx
 from . import _ext
 from .ortho import (
     WORKSPACE,
@@ -109,6 +110,13 @@ def fused_muon_update(
         ):
             groups[key].append((pp, gp, bp, vp[j] if vp is not None else None))
 
+    with nvtx(f"dmb.muon_fused[{R}x{C}]"):
+        _run_groups(C_, groups, lay, R, C, device, fac, eps, ns_steps, strategy, momentum, nesterov, maximize,
+                    weight_decay, cautious_wd, variances, muon_beta2, momentum_done)
+
+
+def _run_groups(C_, groups, lay, R, C, device, fac, eps, ns_steps, strategy, momentum, nesterov, maximize,
+                weight_decay, cautious_wd, variances, muon_beta2, momentum_done):
     for (lr_eff, pdt, gdt), entries in groups.items():
         chunk = batch_chunk(lay, len(entries))
         for s in range(0, len(entries), chunk):

@@ -23,6 +23,7 @@ from torch.distributed.tensor import DTensor, Shard
 
 from ..ops import _ext
 from ..ops.ortho import WORKSPACE, coefficient_table, dtype_code, layout_for, norm_factor
+from ..utils.tracing import nvtx
 from . import symm
 
 # Cap on one owner's share of the symmetric workspace (two ping-pong buffers).
@@ -148,9 +149,10 @@ def _run_batch(C_, ws, sel, params, grads, buffers, variances, lr_eff, lay, R, C
     ]
     floats = [float(momentum), float(lr_eff), float(weight_decay)]
 
-    ws.barrier()  # every reader of the previous batch's results is done
-    C_.dist_pack(meta64, meta32, peer_base, ints, floats, True, has_var)
-    ws.barrier()  # all shards have landed in the owners' workspaces
+    with nvtx("dmb.owner.pack"):
+        ws.barrier()  # every reader of the previous batch's results is done
+        C_.dist_pack(meta64, meta32, peer_base, ints, floats, True, has_var)
+        ws.barrier()  # all shards have landed in the owners' workspaces
 
     mine = max(0, min(Bo, S - rank * Bo))
     if mine > 0:
@@ -170,8 +172,9 @@ def _run_batch(C_, ws, sel, params, grads, buffers, variances, lr_eff, lay, R, C
             vptrs = torch.tensor([vbase + s * R * 4 for s in range(mine)], dtype=torch.int64).pin_memory()
             rowscale = C_.normuon_finalize(rowsq, vptrs.to(device, non_blocking=True), C, muon_beta2)
             region(rs_off, mine * R * 4, torch.float32, (mine, R)).copy_(rowscale)
-    ws.barrier()  # owners' results are ready
-    C_.dist_apply(meta64, meta32, peer_base, ints, floats, has_var)
+    with nvtx("dmb.owner.apply"):
+        ws.barrier()  # owners' results are ready
+        C_.dist_apply(meta64, meta32, peer_base, ints, floats, has_var)
 
 
 def fsdp3d_local_eligible(params, grads, buffers) -> bool:
