@@ -61,11 +61,16 @@ _register_dtensor_foreach_ops()
 
 def _group_muon_tensors(params, grads, state_lists, lr_ratios):
     """Split a group into homogeneous (device, dtype, shape) batches, keeping order."""
-    by_dev: dict[tuple[torch.device, torch.dtype], list[int]] = {}
+    # DTensors are also split by placements and stride: a batch is stacked and
+    # redistributed as one tensor, so e.g. column- and row-parallel TP weights of
+    # the same shape must not share a batch.
+    by_dev: dict[tuple, list[int]] = {}
     for i, p in enumerate(params):
-        by_dev.setdefault((p.device, p.dtype), []).append(i)
+        g = grads[i]
+        layout = (tuple(g.placements), tuple(g.stride())) if hasattr(g, "placements") else None
+        by_dev.setdefault((p.device, p.dtype, layout), []).append(i)
     out = []
-    for (device, _), idxs in by_dev.items():
+    for (device, _, _), idxs in by_dev.items():
         shapes = group_tensors_by_shape([grads[i] for i in idxs])
         for _, (_, local) in shapes.items():
             sel = [idxs[j] for j in local]

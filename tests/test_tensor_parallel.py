@@ -50,3 +50,21 @@ def _worker(rank, world):
 
 def test_tp_normuon_matches_single_process_gloo():
     run_distributed(_worker, 2)
+
+
+def _mixed_worker(rank, world):
+    import torch
+    from torch.distributed.device_mesh import init_device_mesh
+    from torch.distributed.tensor import Shard, distribute_tensor
+
+    from dtensor_muon_b200.optim.optim import _group_muon_tensors
+
+    mesh = init_device_mesh("cpu", (world,))
+    ps = [distribute_tensor(torch.randn(8, 8), mesh, [pl]) for pl in (Shard(0), Shard(1), Shard(0))]
+    groups = _group_muon_tensors(ps, ps, {"momentum_buffer": ps}, [torch.tensor(1.0)] * 3)
+    sizes = sorted(len(g[1]) for g in groups)
+    assert sizes == [1, 2], sizes  # Shard(0) pair together, Shard(1) alone
+
+
+def test_same_shape_different_placements_batch_separately():
+    run_distributed(_mixed_worker, 2)
