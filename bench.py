@@ -102,7 +102,9 @@ def init_dist(gpus: int):
         raise SystemExit(f"--gpus {gpus} but WORLD_SIZE={world}; launch N>1 with torch.distributed.run")
     torch.cuda.set_device(local)
     if world > 1:
-        dist.init_process_group("nccl", device_id=torch.device("cuda", local))
+        import datetime
+
+        dist.init_process_group("nccl", device_id=torch.device("cuda", local), timeout=datetime.timedelta(minutes=5))
     return rank, world, local
 
 
@@ -207,6 +209,20 @@ def build_reference(args, world, device):
 
 # ------------------------------------------------------------------- main --
 def main():
+    args = parse_args()
+    if args.impl != "reference":
+        return run(args)
+    try:
+        return run(args)
+    except Exception as exc:  # the reference failed after it was built: report, do not hang the job
+        rank = int(os.environ.get("RANK", "0"))
+        if rank == 0:
+            print(json.dumps({"impl": "reference", "unavailable": f"{type(exc).__name__}: {exc}"[:300]}), flush=True)
+        if dist.is_initialized():
+            os._exit(0)  # peers may be blocked in a collective; leave without a teardown barrier
+
+
+def parse_args():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=10)
@@ -225,7 +241,10 @@ def main():
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
+    return args
 
+
+def run(args):
     rank, world, local = init_dist(args.gpus)
     device = torch.device("cuda", local)
     par = f"fsdp{world}" if world > 1 else "single"
