@@ -131,7 +131,8 @@ def build_ours(args, world, device):
 
         mesh = init_device_mesh("cuda", (world,))
     model = build_llama(cfg, device, mesh=mesh, seed=0, fsdp_comm=args.fsdp_comm)
-    opt = build_optimizer(model, Muon, lr=args.lr, wd=0.1, orthogonalization_strategy=args.strategy)
+    opt = build_optimizer(model, Muon, lr=args.lr, wd=0.1, orthogonalization_strategy=args.strategy,
+                          fuse_momentum=world > 1 and args.fsdp_comm == "p2p" and args.fuse_momentum)
     from dtensor_muon_b200.models.llama import lm_loss
 
     def step(tokens, targets):
@@ -234,6 +235,8 @@ def parse_args():
     ap.add_argument("--lr", type=float, default=1e-3)
     ap.add_argument("--strategy", default="polar_express")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--fuse-momentum", type=int, default=int(os.environ.get("DMB_FUSE_MOMENTUM", "1")),
+                    help="ours, N > 1: Muon momentum update inside the FSDP gradient reduce-scatter")
     ap.add_argument("--fsdp-comm", default=os.environ.get("DMB_FSDP_COMM", "p2p"), choices=["p2p", "nccl"],
                     help="ours: FSDP collectives on NVLink P2P kernels or NCCL")
     ap.add_argument("--ref-batch-size", type=int, default=32,

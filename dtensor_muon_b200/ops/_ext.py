@@ -37,6 +37,7 @@ _LAUNCHES = {
     "fsdp_reduce_scatter_pull": 1,
     "push_slots": 1,
     "local_slot_sum": 1,
+    "rs_sum_momentum": 1,
     "ep_scatter_rows": 1,
     "ep_gather_rows": 1,
     "rope": 1,

@@ -678,3 +678,79 @@ void local_slot_sum(at::Tensor& out, const at::Tensor& staging_bytes, int64_t of
 }
 
 }  // namespace dmb
+
+// ---- reduce-scatter fused with the Muon momentum update (FSDP backward) ----
+namespace dmb {
+namespace {
+
+constexpr int MAX_SEGS = 64;
+
+// seg table (int64 x 5 per segment): offset, numel (valid, unpadded), momentum buffer
+// pointer (0: not a Muon parameter), flags (bit0 nesterov, bit1 maximize), momentum as
+// float bits. Offsets and numels are multiples of 8.
+__global__ void rs_sum_momentum_kernel(void* __restrict__ out, const void* __restrict__ staging, long long n,
+                                       int world, int dt, float scale, const int64_t* __restrict__ segs, int nseg) {
+  __shared__ int64_t s_off[MAX_SEGS + 1], s_num[MAX_SEGS], s_buf[MAX_SEGS], s_flag[MAX_SEGS];
+  __shared__ float s_mom[MAX_SEGS];
+  for (int i = threadIdx.x; i < nseg; i += blockDim.x) {
+    s_off[i] = segs[i * 5 + 0];
+    s_num[i] = segs[i * 5 + 1];
+    s_buf[i] = segs[i * 5 + 2];
+    s_flag[i] = segs[i * 5 + 3];
+    s_mom[i] = __int_as_float((int)segs[i * 5 + 4]);
+  }
+  if (threadIdx.x == 0) s_off[nseg] = n;
+  __syncthreads();
+  const long long n8 = n / 8;
+  for (long long v = (long long)blockIdx.x * blockDim.x + threadIdx.x; v < n8; v += (long long)gridDim.x * blockDim.x) {
+    const long long e0 = v * 8;
+    float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+    for (int j = 0; j < world; ++j) {
+      float x[8];
+      load8(staging, dt, (long long)j * n + e0, x);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) acc[e] += x[e];
+    }
+#pragma unroll
+    for (int e = 0; e < 8; ++e) acc[e] *= scale;
+    int s = 0;
+    while (s + 1 < nseg && s_off[s + 1] <= e0) ++s;
+    const long long rel = e0 - s_off[s];
+    if (s_buf[s] != 0 && rel < s_num[s]) {
+      float* buf = reinterpret_cast<float*>(s_buf[s]);
+      const float m = s_mom[s];
+      const bool nesterov = s_flag[s] & 1, maximize = (s_flag[s] >> 1) & 1;
+      float b[8];
+      load8(buf, 0, rel, b);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        const float g = maximize ? -acc[e] : acc[e];
+        b[e] = fmaf(b[e], m, g);
+        acc[e] = nesterov ? fmaf(b[e], m, g) : b[e];
+      }
+      store8(buf, 0, rel, b);
+    }
+    store8(out, dt, e0, acc);
+  }
+}
+
+}  // namespace
+
+void rs_sum_momentum(at::Tensor& out, const at::Tensor& staging_bytes, int64_t off, int64_t world, double scale,
+                     const at::Tensor& segs, int64_t max_ctas) {
+  const at::cuda::CUDAGuard guard(out.device());
+  TORCH_CHECK(out.is_contiguous() && (out.scalar_type() == at::kFloat || out.scalar_type() == at::kBFloat16));
+  TORCH_CHECK(segs.is_cuda() && segs.scalar_type() == at::kLong && segs.dim() == 2 && segs.size(1) == 5);
+  const int nseg = segs.size(0);
+  TORCH_CHECK(nseg >= 1 && nseg <= MAX_SEGS, "rs_sum_momentum: 1..64 segments");
+  const long long n = out.numel();
+  TORCH_CHECK(n % 8 == 0 && off % 16 == 0);
+  if (n == 0) return;
+  const int blocks = (int)std::min<long long>(max_ctas, (n / 8 + 255) / 256);
+  rs_sum_momentum_kernel<<<blocks, 256, 0, at::cuda::getCurrentCUDAStream()>>>(
+      out.data_ptr(), static_cast<const char*>(staging_bytes.data_ptr()) + off, n, (int)world,
+      out.scalar_type() == at::kFloat ? 0 : 1, (float)scale, segs.data_ptr<int64_t>(), nseg);
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+}  // namespace dmb

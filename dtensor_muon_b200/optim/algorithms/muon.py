@@ -41,10 +41,25 @@ def distributed_fused(params, grads, buffers, lr_ratios, lr, split_sizes, ns_ste
         return False
     from ...parallel import owner_compute
 
+    from ...parallel.fsdp_comm import FUSED_GRADS
+
     effs = lr_effs(lr, lr_ratios)
+    fused = [id(p) in FUSED_GRADS for p in params]
     if owner_compute.eligible(params, grads, buffers, variances):
-        owner_compute.owner_compute_update(params, grads, buffers, effs, ns_steps=ns_steps, variances=variances, **kw)
+        # Grads whose momentum was applied inside the FSDP reduce-scatter hold g'.
+        for done in (False, True):
+            idx = [i for i, f in enumerate(fused) if f == done]
+            if not idx:
+                continue
+            pick = lambda xs: [xs[i] for i in idx] if xs is not None else None  # noqa: E731
+            owner_compute.owner_compute_update(
+                pick(params), pick(grads), pick(buffers), pick(effs), ns_steps=ns_steps, variances=pick(variances),
+                momentum_done=done, **kw,
+            )
+        FUSED_GRADS.difference_update(id(p) for p in params)
         return True
+    if any(fused):
+        raise RuntimeError("gradients with fused momentum reached a non-fused Muon path")
     if owner_compute.fsdp3d_local_eligible(params, grads, buffers) and (
         variances is None or all(hasattr(v, "to_local") for v in variances)
     ):

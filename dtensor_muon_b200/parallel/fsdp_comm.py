@@ -57,11 +57,21 @@ class _PushStaging:
         return ws, buf, peers, off
 
 
+_STAGING: dict[str, _PushStaging] = {}
+
+
+def _staging(purpose: str) -> _PushStaging:
+    # One staging (one double-buffer parity) per purpose, shared by every FSDP module.
+    if purpose not in _STAGING:
+        _STAGING[purpose] = _PushStaging(purpose)
+    return _STAGING[purpose]
+
+
 class P2PAllGather(AllGather):
     """All-gather by P2P stores: shard -> slot ``rank`` of every peer's staging."""
 
     def __init__(self):
-        self._stage = _PushStaging("fsdp_ag")
+        self._stage = _staging("fsdp_ag")
 
     def allocate(self, size, *, dtype, device):
         return torch.empty(*size, dtype=dtype, device=device)
@@ -80,10 +90,17 @@ class P2PAllGather(AllGather):
 
 
 class P2PReduceScatter(ReduceScatter):
-    """Reduce-scatter by P2P stores: chunk k -> slot ``rank`` of peer k, then a local fp32 sum."""
+    """Reduce-scatter by P2P stores: chunk k -> slot ``rank`` of peer k, then a local fp32 sum.
 
-    def __init__(self):
-        self._stage = _PushStaging("fsdp_rs")
+    With a :class:`FusedMomentum` attached (one instance per FSDP module), the
+    local sum also applies the Muon momentum / Nesterov update of that module's
+    Muon parameters (``rs_sum_momentum``) and leaves g' as their gradient.
+    """
+
+    def __init__(self, module=None, fused=None):
+        self._stage = _staging("fsdp_rs")
+        self._module = module
+        self._fused = fused
 
     def allocate(self, size, *, dtype, device):
         return torch.empty(*size, dtype=dtype, device=device)
@@ -106,24 +123,90 @@ class P2PReduceScatter(ReduceScatter):
         C = _ext.load()
         C.push_slots(input_tensor, peers, off, slot, ws.rank, world, True, COMM_CTAS)
         ws.barrier()  # every rank's chunk for me has landed
-        C.local_slot_sum(output_tensor, buf, off, world, scale, 2 * COMM_CTAS)
+        segs = self._fused.segments(self._module, output_tensor, world) if self._fused is not None else None
+        if segs is not None:
+            C.rs_sum_momentum(output_tensor, buf, off, world, scale, segs, 2 * COMM_CTAS)
+        else:
+            C.local_slot_sum(output_tensor, buf, off, world, scale, 2 * COMM_CTAS)
         return None
 
 
-def use_p2p_collectives(model: torch.nn.Module) -> int:
+# Parameters whose current .grad already holds the Nesterov input g' (their
+# momentum buffer was updated inside the reduce-scatter). The optimizer consumes
+# and clears the marks in its next step.
+FUSED_GRADS: set[int] = set()
+
+
+class FusedMomentum:
+    """Maps each FSDP module's reduce-scatter output to its Muon parameters' momentum buffers.
+
+    Fusion applies to 2-D, dim-0-sharded Muon parameters on a 1-D mesh whose
+    momentum buffer already exists (from the first optimizer step on) and
+    whose gradient is not being accumulated (no ``.grad`` when the reduce-
+    scatter runs). Every other parameter gets the plain reduced gradient.
+    """
+
+    def __init__(self, optimizer):
+        self.opt = optimizer
+        self.group_of = {id(p): g for g in optimizer.param_groups for p in g["params"]}
+
+    def segments(self, module, output: torch.Tensor, world: int):
+        try:
+            fsdp_params = module._get_fsdp_state()._fsdp_param_group.fsdp_params
+        except AttributeError:  # private FSDP2 layout changed: no fusion
+            return None
+        rows, off, fused_ids = [], 0, []
+        for fp in fsdp_params:
+            p = fp.sharded_param
+            shape = tuple(p.shape)
+            padded0 = -(-shape[0] // world) * world
+            rest = 1
+            for d in shape[1:]:
+                rest *= d
+            seg = padded0 * rest // world
+            local = p.to_local()
+            buf_ptr, flags, mom = 0, 0, 0.0
+            g = self.group_of.get(id(p))
+            st = self.opt.state.get(p, {})
+            mb = st.get("momentum_buffer") if st else None
+            if (
+                g is not None and g.get("use_muon") and mb is not None and p.grad is None and len(shape) == 2
+                and not g.get("flatten") and g.get("split_sizes") is None and hasattr(mb, "to_local")
+                and mb.to_local().dtype == torch.float32 and mb.to_local().is_contiguous()
+                and mb.to_local().numel() == local.numel() and local.numel() % 8 == 0 and off % 8 == 0
+                and output.dtype == p.dtype and mb.to_local().data_ptr() % 16 == 0
+            ):
+                buf_ptr = mb.to_local().data_ptr()
+                flags = int(bool(g["nesterov"])) | (int(bool(g["maximize"])) << 1)
+                mom = float(g["momentum"])
+                fused_ids.append(id(p))
+            import struct
+
+            rows.append([off, local.numel(), buf_ptr, flags, struct.unpack("<i", struct.pack("<f", mom))[0]])
+            off += seg
+        if not fused_ids or off != output.numel() or len(rows) > 64 or any(r[0] % 8 for r in rows):
+            return None
+        FUSED_GRADS.update(fused_ids)
+        return torch.tensor(rows, dtype=torch.int64).pin_memory().to(output.device, non_blocking=True)
+
+
+def use_p2p_collectives(model: torch.nn.Module, optimizer=None) -> int:
     """Install the P2P all-gather / reduce-scatter on every FSDP module of ``model``.
 
+    With ``optimizer`` (a Muon), the reduce-scatter also runs the momentum
+    update of the module's Muon parameters (see :class:`FusedMomentum`).
     Returns the number of FSDP modules configured (0 when symmetric memory is unavailable).
     """
     from torch.distributed.fsdp import FSDPModule
 
     if not symm.available():
         return 0
-    ag, rs = P2PAllGather(), P2PReduceScatter()
+    ag = P2PAllGather()
+    fused = FusedMomentum(optimizer) if optimizer is not None else None
     n = 0
     for m in model.modules():
         if isinstance(m, FSDPModule):
             m.set_custom_all_gather(ag)
-            m.set_custom_reduce_scatter(rs)
+            m.set_custom_reduce_scatter(P2PReduceScatter(m, fused))
             n += 1
     return n

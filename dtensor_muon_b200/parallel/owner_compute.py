@@ -81,7 +81,10 @@ def owner_compute_update(
     eps: float = 1e-7,
     variances: list[DTensor] | None = None,
     muon_beta2: float = 0.95,
+    momentum_done: bool = False,
 ) -> None:
+    """``momentum_done``: the grads already hold g' (momentum updated in the
+    FSDP reduce-scatter), so the pack only casts and scatters them."""
     C_ = _ext.load()
     coeffs = coefficient_table(strategy, ns_steps)
     mesh = grads[0].device_mesh
@@ -109,12 +112,13 @@ def owner_compute_update(
             _run_batch(
                 C_, ws, sel, params, grads, buffers, variances, lr_eff, lay, R, C, r0, r1, g1, rank, world,
                 coeffs, fac, eps, weight_decay, cautious_wd, momentum, nesterov, maximize, muon_beta2, has_var,
-                device,
+                device, momentum_done,
             )
 
 
 def _run_batch(C_, ws, sel, params, grads, buffers, variances, lr_eff, lay, R, C, r0, r1, g1, rank, world, coeffs,
-               fac, eps, weight_decay, cautious_wd, momentum, nesterov, maximize, muon_beta2, has_var, device):
+               fac, eps, weight_decay, cautious_wd, momentum, nesterov, maximize, muon_beta2, has_var, device,
+               momentum_done=False):
     S = len(sel)
     Bo = math.ceil(S / world)
     steps = coeffs.shape[0]
@@ -144,14 +148,14 @@ def _run_batch(C_, ws, sel, params, grads, buffers, variances, lr_eff, lay, R, C
         x_off, res_off, sums_off, vbuf_off, rs_off,
         dtype_code(grads[sel[0]].dtype), dtype_code(params[sel[0]].dtype),
         R, C, int(lay.transpose), lay.Np, lay.Mp, r0, r1, g1, rank, world,
-        int(nesterov), int(maximize), int(cautious_wd), int(has_var),
+        int(nesterov), 0 if momentum_done else int(maximize), int(cautious_wd), int(has_var),
         int(all(x % 16 == 0 for row in ptrs[:3] for x in row)),
     ]
     floats = [float(momentum), float(lr_eff), float(weight_decay)]
 
     with nvtx("dmb.owner.pack"):
         ws.barrier()  # every reader of the previous batch's results is done
-        C_.dist_pack(meta64, meta32, peer_base, ints, floats, True, has_var)
+        C_.dist_pack(meta64, meta32, peer_base, ints, floats, not momentum_done, has_var)
         ws.barrier()  # all shards have landed in the owners' workspaces
 
     mine = max(0, min(Bo, S - rank * Bo))

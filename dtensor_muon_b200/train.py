@@ -66,8 +66,14 @@ def build_llama(
 
 
 def build_optimizer(model: nn.Module, optimizer_cls=Muon, lr: float = 1e-3, wd: float = 0.1,
-                    adam_lr: float | None = None, muon_group: dict | None = None, **kwargs):
-    """Muon on the 2-D / 3-D decoder weights, AdamW on embeddings, norms and head."""
+                    adam_lr: float | None = None, muon_group: dict | None = None, fuse_momentum: bool = False,
+                    **kwargs):
+    """Muon on the 2-D / 3-D decoder weights, AdamW on embeddings, norms and head.
+
+    ``fuse_momentum=True`` (FSDP models on the P2P collectives) moves the Muon
+    momentum / Nesterov update into FSDP's gradient reduce-scatter, so it runs
+    during backward; requires one backward per optimizer step.
+    """
     muon, adam = muon_and_adam_params(model)
     groups = [dict(params=muon, **(muon_group or {}))]
     if adam:
@@ -75,7 +81,12 @@ def build_optimizer(model: nn.Module, optimizer_cls=Muon, lr: float = 1e-3, wd: 
         if adam_lr is not None:
             g["lr"] = adam_lr
         groups.append(g)
-    return optimizer_cls(groups, lr=lr, wd=wd, **kwargs)
+    opt = optimizer_cls(groups, lr=lr, wd=wd, **kwargs)
+    if fuse_momentum:
+        from .parallel.fsdp_comm import use_p2p_collectives
+
+        use_p2p_collectives(model, opt)
+    return opt
 
 
 def synthetic_batch(batch: int, seq: int, vocab: int, generator: torch.Generator | None = None,

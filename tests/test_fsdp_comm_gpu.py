@@ -1,4 +1,5 @@
-"""FSDP2 with the P2P all-gather / reduce-scatter kernels against FSDP2 on NCCL (2 GPUs)."""
+"""FSDP2 with the P2P all-gather / reduce-scatter kernels (and with the Muon momentum
+fused into the reduce-scatter) against FSDP2 on NCCL (2 GPUs)."""
 
 import pytest
 import torch
@@ -20,9 +21,9 @@ def _worker(rank, world):
     cfg = preset("tiny", vocab_size=1024, dim=256, n_layers=2)
     dev = torch.device("cuda", rank)
     results = {}
-    for comm in ("nccl", "p2p"):
-        model = build_llama(cfg, dev, mesh=mesh, seed=0, fsdp_comm=comm)
-        opt = build_optimizer(model, lr=1e-2)
+    for comm in ("nccl", "p2p", "p2p+fused"):
+        model = build_llama(cfg, dev, mesh=mesh, seed=0, fsdp_comm=comm.split("+")[0])
+        opt = build_optimizer(model, lr=1e-2, fuse_momentum=comm.endswith("fused"))
         gen = torch.Generator().manual_seed(7 + rank)
         losses = []
         for _ in range(3):
@@ -30,16 +31,20 @@ def _worker(rank, world):
             loss = lm_loss(model(ids[:, :-1]), ids[:, 1:])
             loss.backward()
             opt.step()
-            opt.zero_grad()
+            opt.zero_grad(set_to_none=True)
             losses.append(loss.item())
         results[comm] = (losses, [p.full_tensor().float() for p in model.parameters()])
     torch.cuda.synchronize()
     _ext.check_device_errors(dev)
-    for a, b in zip(results["nccl"][0], results["p2p"][0]):
-        assert abs(a - b) < 2e-2 * max(1.0, abs(a)), (a, b)
-    for x, y in zip(results["nccl"][1], results["p2p"][1]):
-        bad = (~torch.isclose(x, y, rtol=2e-2, atol=2e-2)).float().mean().item()
-        assert bad < 0.02, bad
+    from dtensor_muon_b200.parallel.fsdp_comm import FUSED_GRADS
+
+    assert not FUSED_GRADS, "every fused gradient must be consumed by an optimizer step"
+    for other in ("p2p", "p2p+fused"):
+        for a, b in zip(results["nccl"][0], results[other][0]):
+            assert abs(a - b) < 2e-2 * max(1.0, abs(a)), (other, a, b)
+        for x, y in zip(results["nccl"][1], results[other][1]):
+            bad = (~torch.isclose(x, y, rtol=2e-2, atol=2e-2)).float().mean().item()
+            assert bad < 0.02, (other, bad)
 
 
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
