@@ -235,7 +235,7 @@ def parse_args():
     ap.add_argument("--lr", type=float, default=1e-3)
     ap.add_argument("--strategy", default="polar_express")
     ap.add_argument("--no-e2e", action="store_true")
-    ap.add_argument("--fuse-momentum", type=int, default=int(os.environ.get("DMB_FUSE_MOMENTUM", "1")),
+    ap.add_argument("--fuse-momentum", type=int, default=int(os.environ.get("DMB_FUSE_MOMENTUM", "0")),
                     help="ours, N > 1: Muon momentum update inside the FSDP gradient reduce-scatter")
     ap.add_argument("--fsdp-comm", default=os.environ.get("DMB_FSDP_COMM", "p2p"), choices=["p2p", "nccl"],
                     help="ours: FSDP collectives on NVLink P2P kernels or NCCL")

@@ -129,6 +129,16 @@ def foreach_zeropower(
         Gs_d = cast(list[DTensor], Gs)
         meta = get_dtensor_metadata(Gs_d)
         mesh = meta["device_mesh"]
+        if _needs_gather_path(meta["placements"]):
+            # FSDP over TP-sharded weights (_StridedShard + Shard): gather each
+            # full matrix, orthogonalise the batch locally, hand back shards.
+            full = torch.stack([g.full_tensor() for g in Gs_d])
+            U = orthogonalize_local(full, steps, eps, strategy, use_native)
+            rep = (Replicate(),) * mesh.ndim
+            return [
+                DTensor.from_local(u, device_mesh=mesh, placements=rep).redistribute(placements=meta["placements"])
+                for u in U.unbind(0)
+            ]
         owner_pl = (Shard(0), *([Replicate()] * (mesh.ndim - 1)))
         X = cast(DTensor, torch.stack(list(Gs_d), dim=0).bfloat16())
         X_own = X.redistribute(placements=owner_pl, async_op=True)
@@ -139,6 +149,11 @@ def foreach_zeropower(
     X = torch.stack(list(Gs))
     U = orthogonalize_local(X, steps, eps, strategy, use_native)
     return list(U.unbind(0))
+
+
+def _needs_gather_path(placements) -> bool:
+    """Placements the stacked redistribute cannot express (strided shards from FSDP x TP)."""
+    return any(type(p).__name__ == "_StridedShard" for p in placements)
 
 
 def is_fsdp_3d_sharded(xs: list[Tensor]) -> bool:

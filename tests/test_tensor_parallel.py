@@ -68,3 +68,44 @@ def _mixed_worker(rank, world):
 
 def test_same_shape_different_placements_batch_separately():
     run_distributed(_mixed_worker, 2)
+
+
+def _fsdp_tp_worker(rank, world):
+    import torch
+    from torch.distributed.device_mesh import init_device_mesh
+
+    from dtensor_muon_b200 import Muon
+    from dtensor_muon_b200.models.llama import Llama, lm_loss, muon_and_adam_params, preset
+    from dtensor_muon_b200.parallel.tensor_parallel import apply_fsdp_tp
+
+    cfg = preset("tiny")
+    torch.manual_seed(0)
+    ref = Llama(cfg)
+    ref.init_weights(seed=0)
+    model = Llama(cfg)
+    model.load_state_dict(ref.state_dict())
+    mesh = init_device_mesh("cpu", (2, 2), mesh_dim_names=("dp", "tp"))
+    apply_fsdp_tp(model, mesh)
+
+    def make_opt(m):
+        mu, ad = muon_and_adam_params(m)
+        return Muon([{"params": mu, "algorithm": "normuon"}, {"params": ad, "algorithm": "adamw"}],
+                    lr=0.02, orthogonalization_strategy="newton_schulz", foreach=False)
+
+    o_ref, o_m = make_opt(ref), make_opt(model)
+    tok = torch.randint(0, cfg.vocab_size, (2, 17), generator=torch.Generator().manual_seed(3))
+    dp = mesh.get_local_rank("dp")
+    # every dp rank sees the same batch, so the averaged grads equal the single-process ones
+    lm_loss(ref(tok[:, :-1]), tok[:, 1:]).backward()
+    lm_loss(model(tok[:, :-1]), tok[:, 1:]).backward()
+    o_ref.step()
+    o_m.step()
+    refp = dict(ref.named_parameters())
+    for name, p in model.named_parameters():
+        full = p.full_tensor() if hasattr(p, "full_tensor") else p
+        bad = (~torch.isclose(full.detach(), refp[name].detach(), rtol=1e-2, atol=3e-3)).float().mean().item()
+        assert bad < 0.02, (name, bad, dp)
+
+
+def test_fsdp_x_tp_normuon_gloo_four_ranks():
+    run_distributed(_fsdp_tp_worker, 4)
