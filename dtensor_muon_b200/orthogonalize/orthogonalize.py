@@ -133,7 +133,7 @@ def foreach_zeropower(
             # FSDP over TP-sharded weights (_StridedShard + Shard): gather each
             # full matrix, orthogonalise the batch locally, hand back shards.
             full = torch.stack([g.full_tensor() for g in Gs_d])
-            U = orthogonalize_local(full, steps, eps, strategy, use_native)
+            U = _split_over_mesh(full, mesh, lambda x: orthogonalize_local(x, steps, eps, strategy, use_native))
             rep = (Replicate(),) * mesh.ndim
             return [
                 DTensor.from_local(u, device_mesh=mesh, placements=rep).redistribute(placements=meta["placements"])
@@ -149,6 +149,26 @@ def foreach_zeropower(
     X = torch.stack(list(Gs))
     U = orthogonalize_local(X, steps, eps, strategy, use_native)
     return list(U.unbind(0))
+
+
+def _split_over_mesh(full: Tensor, mesh, fn) -> Tensor:
+    """Apply ``fn`` to a replicated batch with the work split over every rank of ``mesh``:
+    rank r handles a contiguous chunk, then one all-gather returns all results."""
+    import torch.distributed as dist
+
+    world = mesh.size()
+    if world == 1 or world != dist.get_world_size():
+        return fn(full)
+    rank = dist.get_rank()
+    B = full.shape[0]
+    chunk = -(-B // world)
+    mine = fn(full[rank * chunk : min(B, (rank + 1) * chunk)]) if rank * chunk < B else None
+    out = torch.empty((chunk * world, *full.shape[1:]), dtype=torch.bfloat16, device=full.device)
+    send = torch.zeros((chunk, *full.shape[1:]), dtype=torch.bfloat16, device=full.device)
+    if mine is not None:
+        send[: mine.shape[0]].copy_(mine)
+    dist.all_gather_into_tensor(out, send)
+    return out[:B]
 
 
 def _needs_gather_path(placements) -> bool:
