@@ -98,6 +98,21 @@ def _fsdp_tp_worker(rank, world):
     # every dp rank sees the same batch, so the averaged grads equal the single-process ones
     lm_loss(ref(tok[:, :-1]), tok[:, 1:]).backward()
     lm_loss(model(tok[:, :-1]), tok[:, 1:]).backward()
+    # batched path on the strided-shard grads (FSDP over TP): gather + split-over-mesh
+    from dtensor_muon_b200.orthogonalize import foreach_zeropower, orthogonalize_local
+
+    strided = [p.grad for p in model.parameters()
+               if p.grad is not None and p.ndim == 2 and any(type(q).__name__ == "_StridedShard" for q in p.placements)]
+    assert strided, "expected FSDP x TP strided-shard placements"
+    by_shape = {}
+    for g in strided:
+        by_shape.setdefault((tuple(g.shape), tuple(g.placements)), []).append(g)
+    for gs in by_shape.values():
+        us = foreach_zeropower(gs, steps=5, strategy="newton_schulz")
+        ref_u = orthogonalize_local(torch.stack([g.full_tensor() for g in gs]), 5, 1e-7, "newton_schulz")
+        for u, r in zip(us, ref_u):
+            assert u.placements == gs[0].placements
+            torch.testing.assert_close(u.full_tensor().float(), r.float(), rtol=2e-2, atol=2e-2)
     o_ref.step()
     o_m.step()
     refp = dict(ref.named_parameters())
