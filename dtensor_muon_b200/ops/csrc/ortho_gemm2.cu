@@ -33,7 +33,7 @@ constexpr int STAGES = 6;
 constexpr int A_STAGE = 128 * BK * 2;   // 16 KiB
 constexpr int B_STAGE = 128 * BK * 2;   // 16 KiB (this CTA's half of B)
 constexpr int STAGE_BYTES = A_STAGE + B_STAGE;
-constexpr int THREADS = 192;
+constexpr int THREADS = 320;  // warp 0 TMA, warp 1 MMA, warps 2..9 epilogue
 constexpr int TMEM_COLS = 512;
 constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 + 256;
 
@@ -150,7 +150,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
     }
     for (int a = 0; a < 2; ++a) {
       mbar_init(&tfull[a], 1);
-      mbar_init(&tempty[a], 8);  // 4 epilogue warps x 2 CTAs
+      mbar_init(&tempty[a], 16);  // 8 epilogue warps x 2 CTAs
     }
     *abort_flag = 0;
     fence_mbarrier_init();
@@ -253,7 +253,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
     }
   } else {
     // ---------------------------------------------------------- epilogue --
+    // Two warps per TMEM lane quadrant (warp & 3), each draining half of the
+    // 256 accumulator columns, so short-K tiles are not epilogue-bound.
     const int q = warp & 3;
+    const int half = (warp - 2) >> 2;
     const uint32_t tempty_leader[2] = {map_to_cta(smem_u32(&tempty[0]), 0), map_to_cta(smem_u32(&tempty[1]), 0)};
     int acc = 0;
     uint32_t acc_phase = 0;
@@ -269,7 +272,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
       __nv_bfloat16* out_b = p.out + (long long)b * p.out_bstride;
       const __nv_bfloat16* res_b = p.res ? p.res + (long long)b * p.res_bstride : nullptr;
 #pragma unroll 1
-      for (int c = 0; c < TN / 32; ++c) {
+      for (int c = half * (TN / 64); c < (half + 1) * (TN / 64); ++c) {
         uint32_t r[32];
         tmem_ld_32cols(tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc * TN + c * 32), r);
         const int col0 = tn * TN + c * 32;
