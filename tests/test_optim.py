@@ -350,3 +350,20 @@ def test_mixed_muon_and_adam_groups(monkeypatch):
 
 def test_get_algorithm_is_case_insensitive():
     assert get_algorithm("MUON").name == "muon"
+
+
+def test_outer_torch_compile_of_step_matches_eager(monkeypatch):
+    """An outer torch.compile around step() runs the same update (graph breaks allowed)."""
+    _identity_ortho(monkeypatch)
+    p = torch.nn.Parameter(torch.ones(4, 2))
+    ref = torch.nn.Parameter(p.detach().clone())
+    opt = Muon([p], lr=0.1, wd=0.0, momentum=0.0, nesterov=False)
+    ref_opt = Muon([ref], lr=0.1, wd=0.0, momentum=0.0, nesterov=False)
+    compiled = torch.compile(opt.step, backend="eager")
+    for value in (0.5, 0.25):
+        p.grad = torch.full_like(p, value)
+        ref.grad = torch.full_like(ref, value)
+        compiled()
+        ref_opt.step()
+    torch.testing.assert_close(p, ref)
+    torch.testing.assert_close(opt.state[p]["momentum_buffer"], ref_opt.state[ref]["momentum_buffer"])

@@ -158,3 +158,18 @@ def test_muon_step_uses_native_kernels():
     n0 = _ext.launch_count
     _run(opt, a, steps=1)
     assert _ext.launch_count - n0 >= len(set(SHAPES)) * 15
+
+
+def test_fused_adam_group_keeps_step_on_device_and_matches_torch():
+    g = torch.Generator().manual_seed(0)
+    a = [nn.Parameter(torch.randn(64, generator=g).cuda())]
+    b = [nn.Parameter(a[0].detach().clone())]
+    opt = Muon([{"params": a, "algorithm": "adamw", "fused": True, "lr": 0.01}])
+    ref = torch.optim.AdamW(b, lr=0.01, weight_decay=0.1, betas=(0.9, 0.95), fused=True)
+    for _ in range(2):
+        gr = torch.randn(64, generator=g).cuda()
+        a[0].grad, b[0].grad = gr.clone(), gr.clone()
+        opt.step()
+        ref.step()
+    assert opt.state[a[0]]["step"].device == a[0].device
+    torch.testing.assert_close(a[0], b[0])
