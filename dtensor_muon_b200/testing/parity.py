@@ -23,7 +23,9 @@ import torch
 ROOT = os.path.dirname(os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
 
 
-def run(impl: str, steps: int = 20) -> dict:
+def run(impl: str, steps: int = 20, load: str | None = None, save: str | None = None, start: int = 0) -> dict:
+    """Train ``steps`` steps (data steps ``start`` .. ``start + steps``); optionally
+    resume model + optimizer from ``load`` and write them to ``save`` (torch.save)."""
     sys.path.insert(0, ROOT)
     from dtensor_muon_b200.models.llama import Llama, lm_loss, muon_and_adam_params, preset
 
@@ -48,16 +50,22 @@ def run(impl: str, steps: int = 20) -> dict:
         from dtensor_muon_b200 import Muon
 
         opt = Muon(groups, **kw)
+    if load:
+        ckpt = torch.load(load, weights_only=False)
+        model.load_state_dict(ckpt["model"])
+        opt.load_state_dict(ckpt["optim"])
     gen = torch.Generator().manual_seed(0)
-    ids = torch.randint(0, cfg.vocab_size, (steps, 8, 129), generator=gen)
+    ids = torch.randint(0, cfg.vocab_size, (start + steps, 8, 129), generator=gen)
     losses = []
-    for s in range(steps):
+    for s in range(start, start + steps):
         loss = lm_loss(model(ids[s, :, :-1]), ids[s, :, 1:])
         loss.backward()
         opt.step()
         opt.zero_grad()
         losses.append(loss.item())
     checksum = float(sum(p.detach().double().abs().sum() for p in model.parameters()))
+    if save:
+        torch.save({"model": model.state_dict(), "optim": opt.state_dict()}, save)
     return {"impl": impl, "losses": losses, "param_abs_sum": checksum}
 
 
@@ -65,8 +73,11 @@ def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--start", type=int, default=0)
+    ap.add_argument("--load")
+    ap.add_argument("--save")
     args = ap.parse_args()
-    print(json.dumps(run(args.impl, args.steps)))
+    print(json.dumps(run(args.impl, args.steps, args.load, args.save, args.start)))
 
 
 if __name__ == "__main__":

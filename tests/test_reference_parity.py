@@ -11,10 +11,10 @@ ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
 REF = os.path.join(ROOT, "baseline", "_ref", "muonium")
 
 
-def _run(impl):
+def _run(impl, *extra):
     env = dict(os.environ, TORCH_COMPILE_DISABLE="1", CUDA_VISIBLE_DEVICES="")
     out = subprocess.run(
-        [sys.executable, "-m", "dtensor_muon_b200.testing.parity", "--impl", impl],
+        [sys.executable, "-m", "dtensor_muon_b200.testing.parity", "--impl", impl, *extra],
         cwd=ROOT, env=env, capture_output=True, text=True, timeout=600,
     )
     assert out.returncode == 0, out.stderr[-2000:]
@@ -28,3 +28,16 @@ def test_losses_and_params_match_reference_cpu():
     for a, b in zip(ours["losses"], ref["losses"]):
         assert abs(a - b) <= 1e-4 * max(1.0, abs(b)), (a, b)
     assert abs(ours["param_abs_sum"] - ref["param_abs_sum"]) <= 1e-5 * ref["param_abs_sum"]
+
+
+@pytest.mark.skipif(not os.path.isdir(REF), reason="reference not installed under baseline/_ref")
+@pytest.mark.parametrize("first,second", [("reference", "ours"), ("ours", "reference")])
+def test_checkpoint_round_trip_with_reference(tmp_path, first, second):
+    """A checkpoint written by one implementation resumes identically in the other."""
+    path = str(tmp_path / "ckpt.pt")
+    _run(first, "--steps", "5", "--save", path)
+    resumed = _run(second, "--steps", "5", "--start", "5", "--load", path)
+    straight = _run(first, "--steps", "10")
+    for a, b in zip(resumed["losses"], straight["losses"][5:]):
+        assert abs(a - b) <= 1e-4 * max(1.0, abs(b)), (a, b)
+    assert abs(resumed["param_abs_sum"] - straight["param_abs_sum"]) <= 1e-5 * straight["param_abs_sum"]
