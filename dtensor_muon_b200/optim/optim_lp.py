@@ -277,11 +277,27 @@ class MuonLP(Muon):
             return super().muon(algorithm, params, grads, state, lr_ratios, **kw)
         opts = {k: v for k, v in kw.items() if k not in ("foreach",)}
         pending: dict[tuple, list[int]] = {}
+        fused: dict[tuple, list[tuple]] = {}
         for i, (p, g, r) in enumerate(zip(params, grads, lr_ratios, strict=True)):
             st = {k: v[i] for k, v in state.items()}
-            if self._fused_lp(algorithm, p, g, st, r, opts):
+            item = self._fused_lp(algorithm, p, g, st, r, opts)
+            if item is not None:
+                pl, ge, var, _ = item
+                fused.setdefault((tuple(ge.shape), pl.dtype, var is not None), []).append(item)
                 continue
             pending.setdefault((tuple(g.shape), g.dtype, str(g.device)), []).append(i)
+        # Quantised momentum already stepped per tensor (lp_momentum_step); the
+        # orthogonalisation + apply run batched per shape.
+        for items in fused.values():
+            ps, gs, vs = [it[0] for it in items], [it[1] for it in items], [it[2] for it in items]
+            effs = [it[3] for it in items]
+            muon_fused.fused_muon_update(
+                ps, gs, gs, effs,
+                weight_decay=opts["weight_decay"], cautious_wd=opts["cautious_wd"], momentum=0.0, nesterov=False,
+                maximize=False, ns_steps=opts["ns_steps"], strategy=opts["orthogonalization_strategy"],
+                variances=vs if vs[0] is not None else None, muon_beta2=opts.get("muon_beta2", 0.95),
+                momentum_done=True,
+            )
         # Generic: dequantise into fp32 temporaries, run the normal (batched when
         # on CUDA) update for a bounded chunk of same-shape tensors, requantise.
         for idxs in pending.values():
@@ -311,53 +327,39 @@ class MuonLP(Muon):
                 for q, t in temps:
                     q.copy_(to_local(t))
 
-    def _fused_lp(self, algorithm, p, g, st, lr_ratio, opts) -> bool:
+    def _fused_lp(self, algorithm, p, g, st, lr_ratio, opts):
+        """Step the quantised momentum of one tensor; returns (param, g', variance, lr_eff)
+        for the batched orthogonalisation, or None when the fused path does not apply."""
         q = st.get("momentum_buffer")
         if not isinstance(q, QuantizedState) or not q.codes.is_cuda:
-            return False
+            return None
         if type(algorithm) not in (MuonBaseline, NorMuon) or not algo_base._seams_are_builtin():
-            return False
+            return None
         if opts.get("split_sizes") is not None:
-            return False
+            return None
         if isinstance(p, DTensor) or isinstance(g, DTensor):
             # Dim-0-sharded 3-D stacks (EP experts): local shards are whole matrices.
             from ..orthogonalize import is_fsdp_3d_sharded
 
             if not (isinstance(p, DTensor) and is_fsdp_3d_sharded([g])):
-                return False
+                return None
             p, g = p.to_local(), g.to_local()
         if not (p.is_contiguous() and g.is_contiguous() and _ext.available()):
-            return False
+            return None
         if p.dtype not in (torch.float32, torch.bfloat16) or g.dtype not in (torch.float32, torch.bfloat16):
-            return False
+            return None
         variances = None
         if isinstance(algorithm, NorMuon):
             v = to_local(st["variance_neuron"])
             if isinstance(v, QuantizedState) or not (v.is_cuda and v.is_contiguous()):
-                return False
+                return None
             variances = [v]
         g_eff = torch.empty(g.shape, dtype=torch.bfloat16, device=g.device)
         _ext.load().lp_momentum_step(
             q.codes, q.scale, q.qmap, q.fmt, q.block_size, g, g_eff, float(opts["momentum"]),
             bool(opts["nesterov"]), bool(opts["maximize"]),
         )
-        muon_fused.fused_muon_update(
-            [p],
-            [g_eff],
-            [g_eff],
-            lr_effs(opts["lr"], [lr_ratio]),
-            weight_decay=opts["weight_decay"],
-            cautious_wd=opts["cautious_wd"],
-            momentum=0.0,
-            nesterov=False,
-            maximize=False,
-            ns_steps=opts["ns_steps"],
-            strategy=opts["orthogonalization_strategy"],
-            variances=variances,
-            muon_beta2=opts.get("muon_beta2", 0.95),
-            momentum_done=True,
-        )
-        return True
+        return p, g_eff, variances[0] if variances is not None else None, lr_effs(opts["lr"], [lr_ratio])[0]
 
 
 class Muon8bit(MuonLP):
