@@ -28,7 +28,21 @@ def shapes(profile):
     return [s for n, s in profile for _ in range(n)]
 
 
-def run(profile) -> str:
+def reference_variants():
+    """The unmodified reference optimizer from baseline/_ref (compiled update, Triton Gram)."""
+    root = os.path.join(os.path.dirname(os.path.dirname(os.path.abspath(__file__))), "baseline", "_ref")
+    if not os.path.isdir(os.path.join(root, "muonium")):
+        return {}
+    sys.path.insert(0, root)
+    from muonium import Muon as RefMuon
+
+    return {
+        "reference Muon per-param (pe)": lambda ps: RefMuon(ps, foreach=False, use_cautious_wd=False),
+        "reference Muon foreach (pe)": lambda ps: RefMuon(ps, foreach=True, use_cautious_wd=False),
+    }
+
+
+def run(profile, with_reference: bool = False) -> str:
     from dtensor_muon_b200 import Muon, Muon4bit, Muon8bit, MuonFp8
 
     sh = shapes(profile)
@@ -46,6 +60,8 @@ def run(profile) -> str:
         "Muon4bit (pe)": lambda ps: Muon4bit(ps, use_cautious_wd=False),
         "MuonFp8 (pe)": lambda ps: MuonFp8(ps, use_cautious_wd=False),
     }
+    if with_reference:
+        variants.update(reference_variants())
     rows = []
     base = None
     for name, make in variants.items():
@@ -66,8 +82,9 @@ def run(profile) -> str:
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--quick", action="store_true")
+    ap.add_argument("--with-reference", action="store_true")
     args = ap.parse_args()
-    print(run(QUICK if args.quick else FULL))
+    print(run(QUICK if args.quick else FULL, args.with_reference))
 
 
 if __name__ == "__main__":

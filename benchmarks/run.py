@@ -27,7 +27,7 @@ def main():
     parts = ["# Benchmark results", "", "```", json.dumps(capture_env(), indent=1), "```", ""]
     parts += ["## Orthogonalisation kernels", "",
               bench_kernels.run(bench_kernels.QUICK if args.quick else bench_kernels.CONFIG2, args.with_reference), ""]
-    parts += ["## optimizer.step()", "", bench_optim.run(bench_optim.QUICK if args.quick else bench_optim.FULL), ""]
+    parts += ["## optimizer.step()", "", bench_optim.run(bench_optim.QUICK if args.quick else bench_optim.FULL, args.with_reference), ""]
     text = "\n".join(parts)
     with open(args.out, "w") as f:
         f.write(text)
