@@ -408,6 +408,11 @@ class Muon(torch.optim.Optimizer):
             split_sizes=split_sizes,
             **opts,
         )
+        if not foreach and self._per_param_can_batch(algorithm, params, state):
+            # The built-in algorithms' per-parameter update is the fp32 math of the
+            # fused kernels, so same-shape CUDA parameters are stepped as one batch
+            # (identical arithmetic, better GPU occupancy).
+            foreach = True
         if not foreach:
             for i, (p, g, r) in enumerate(zip(params, grads, lr_ratios, strict=True)):
                 algorithm.update(p, g, {k: v[i] for k, v in state.items()}, r, **kw)
@@ -435,6 +440,16 @@ class Muon(torch.optim.Optimizer):
                     for o, m in zip(originals, moved, strict=True):
                         if o is not None and m is not None:
                             o.copy_(m.to(o.device))
+
+    @staticmethod
+    def _per_param_can_batch(algorithm, params, state) -> bool:
+        from .algorithms import MuonBaseline, NorMuon
+        from .algorithms import base as _base
+
+        if type(algorithm) not in (MuonBaseline, NorMuon) or not _base._seams_are_builtin():
+            return False
+        tensors = list(params) + [t for ts in state.values() for t in ts]
+        return all(isinstance(t, Tensor) and t.is_cuda and not hasattr(t, "device_mesh") for t in tensors)
 
     def _step_muon_group(self, group: dict) -> None:
         algorithm = get_algorithm(group.get("algorithm", "muon"))
