@@ -43,6 +43,8 @@ _LAUNCHES = {
     "rope": 1,
     "swiglu_fwd": 1,
     "swiglu_bwd": 1,
+    "cross_entropy_fwd": 1,
+    "cross_entropy_bwd": 1,
 }
 launch_count = 0
 

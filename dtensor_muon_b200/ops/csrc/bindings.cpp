@@ -80,6 +80,9 @@ void ep_gather_rows(at::Tensor& dst, const at::Tensor& src_rank, const at::Tenso
 at::Tensor rope(const at::Tensor& x, const at::Tensor& cos_t, const at::Tensor& sin_t, double sign);
 at::Tensor swiglu_fwd(const at::Tensor& a, const at::Tensor& b);
 std::vector<at::Tensor> swiglu_bwd(const at::Tensor& a, const at::Tensor& b, const at::Tensor& dh);
+std::vector<at::Tensor> cross_entropy_fwd(const at::Tensor& logits, const at::Tensor& targets);
+at::Tensor cross_entropy_bwd(const at::Tensor& logits, const at::Tensor& targets, const at::Tensor& lse,
+                             double scale, const c10::optional<at::Tensor>& gscale);
 
 // One status word per device. Kernels whose bounded waits give up write an
 // error code here; the host reads and clears it with take_device_error().
@@ -142,5 +145,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("rope", &dmb::rope);
   m.def("swiglu_fwd", &dmb::swiglu_fwd);
   m.def("swiglu_bwd", &dmb::swiglu_bwd);
+  m.def("cross_entropy_fwd", &dmb::cross_entropy_fwd);
+  m.def("cross_entropy_bwd", &dmb::cross_entropy_bwd);
   m.def("take_device_error", &dmb::take_device_error);
 }

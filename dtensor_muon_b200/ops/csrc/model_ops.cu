@@ -152,3 +152,122 @@ std::vector<at::Tensor> swiglu_bwd(const at::Tensor& a, const at::Tensor& b, con
 }
 
 }  // namespace dmb
+
+// ---- fused cross entropy over bf16 logits [T, V] (mean over rows) ----------
+namespace dmb {
+namespace {
+
+constexpr int CE_THREADS = 512;
+
+__device__ __forceinline__ void ce_merge(float& m, float& s, float m2, float s2) {
+  const float mx = fmaxf(m, m2);
+  s = (m == -INFINITY ? 0.f : s * expf(m - mx)) + (m2 == -INFINITY ? 0.f : s2 * expf(m2 - mx));
+  m = mx;
+}
+
+// One CTA per row: online max / sum-exp over the row (16-byte loads), then
+// loss_row = logsumexp - logit[target]; lse kept for the backward.
+__global__ void __launch_bounds__(CE_THREADS) ce_fwd_kernel(const __nv_bfloat16* __restrict__ logits,
+                                                            const int64_t* __restrict__ targets, int V,
+                                                            float* __restrict__ loss, float* __restrict__ lse) {
+  const long long row = blockIdx.x;
+  const __nv_bfloat16* x = logits + row * (long long)V;
+  float m = -INFINITY, s = 0.f;
+  const int nvec = V / 8;
+  for (int v = threadIdx.x; v < nvec; v += CE_THREADS) {
+    float f[8];
+    load8(x, 1, (long long)v * 8, f);
+    float mm = f[0];
+#pragma unroll
+    for (int k = 1; k < 8; ++k) mm = fmaxf(mm, f[k]);
+    float ss = 0.f;
+#pragma unroll
+    for (int k = 0; k < 8; ++k) ss += expf(f[k] - mm);
+    ce_merge(m, s, mm, ss);
+  }
+  for (int j = nvec * 8 + threadIdx.x; j < V; j += CE_THREADS) ce_merge(m, s, __bfloat162float(x[j]), 1.f);
+  __shared__ float sm[CE_THREADS / 32], ss_[CE_THREADS / 32];
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const float m2 = __shfl_xor_sync(0xffffffffu, m, o), s2 = __shfl_xor_sync(0xffffffffu, s, o);
+    ce_merge(m, s, m2, s2);
+  }
+  const int w = threadIdx.x >> 5, l = threadIdx.x & 31;
+  if (l == 0) {
+    sm[w] = m;
+    ss_[w] = s;
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    float M = sm[0], S = ss_[0];
+    for (int i = 1; i < CE_THREADS / 32; ++i) ce_merge(M, S, sm[i], ss_[i]);
+    const float l_se = M + logf(S);
+    lse[row] = l_se;
+    loss[row] = l_se - __bfloat162float(x[targets[row]]);
+  }
+}
+
+// grad[row, j] = scale * (softmax(row)_j - [j == target]), written as bf16.
+__global__ void __launch_bounds__(256) ce_bwd_kernel(const __nv_bfloat16* __restrict__ logits,
+                                                     const int64_t* __restrict__ targets,
+                                                     const float* __restrict__ lse, int V, float scale,
+                                                     const float* __restrict__ gscale, __nv_bfloat16* __restrict__ grad) {
+  const long long row = blockIdx.y;
+  if (gscale) scale *= *gscale;  // upstream gradient of the mean, read on the device
+  const __nv_bfloat16* x = logits + row * (long long)V;
+  __nv_bfloat16* g = grad + row * (long long)V;
+  const float l_se = lse[row];
+  const long long t = targets[row];
+  const int nvec = V / 8;
+  for (int v = blockIdx.x * blockDim.x + threadIdx.x; v < nvec; v += gridDim.x * blockDim.x) {
+    float f[8];
+    load8(x, 1, (long long)v * 8, f);
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      const long long j = (long long)v * 8 + k;
+      f[k] = scale * (expf(f[k] - l_se) - (j == t ? 1.f : 0.f));
+    }
+    store8(g, 1, (long long)v * 8, f);
+  }
+  if (blockIdx.x == 0)
+    for (int j = nvec * 8 + threadIdx.x; j < V; j += blockDim.x)
+      g[j] = __float2bfloat16_rn(scale * (expf(__bfloat162float(x[j]) - l_se) - (j == t ? 1.f : 0.f)));
+}
+
+}  // namespace
+
+std::vector<at::Tensor> cross_entropy_fwd(const at::Tensor& logits, const at::Tensor& targets) {
+  TORCH_CHECK(logits.is_cuda() && logits.scalar_type() == at::kBFloat16 && logits.is_contiguous() && logits.dim() == 2);
+  TORCH_CHECK(targets.is_cuda() && targets.scalar_type() == at::kLong && targets.numel() == logits.size(0));
+  TORCH_CHECK(reinterpret_cast<uintptr_t>(logits.data_ptr()) % 16 == 0 && logits.size(1) % 8 == 0,
+              "cross_entropy_fwd: 16-byte aligned rows (vocab % 8 == 0) expected");
+  const at::cuda::CUDAGuard guard(logits.device());
+  const int T = logits.size(0), V = logits.size(1);
+  auto loss = at::empty({T}, logits.options().dtype(at::kFloat));
+  auto lse = at::empty({T}, logits.options().dtype(at::kFloat));
+  if (T) {
+    ce_fwd_kernel<<<T, CE_THREADS, 0, at::cuda::getCurrentCUDAStream()>>>(
+        reinterpret_cast<const __nv_bfloat16*>(logits.data_ptr()), targets.data_ptr<int64_t>(), V,
+        loss.data_ptr<float>(), lse.data_ptr<float>());
+    C10_CUDA_KERNEL_LAUNCH_CHECK();
+  }
+  return {loss, lse};
+}
+
+at::Tensor cross_entropy_bwd(const at::Tensor& logits, const at::Tensor& targets, const at::Tensor& lse,
+                             double scale, const c10::optional<at::Tensor>& gscale) {
+  const at::cuda::CUDAGuard guard(logits.device());
+  const int T = logits.size(0), V = logits.size(1);
+  auto grad = at::empty_like(logits);
+  if (T) {
+    const int per_row = std::max(1, std::min(16, (V / 8 + 255) / 256));
+    ce_bwd_kernel<<<dim3(per_row, T), 256, 0, at::cuda::getCurrentCUDAStream()>>>(
+        reinterpret_cast<const __nv_bfloat16*>(logits.data_ptr()), targets.data_ptr<int64_t>(), lse.data_ptr<float>(),
+        V, (float)scale, gscale.has_value() ? gscale->data_ptr<float>() : nullptr,
+        reinterpret_cast<__nv_bfloat16*>(grad.data_ptr()));
+    C10_CUDA_KERNEL_LAUNCH_CHECK();
+  }
+  return grad;
+}
+
+}  // namespace dmb

@@ -63,3 +63,27 @@ def swiglu(a: Tensor, b: Tensor) -> Tensor:
     if _native(a, b) and a.numel() % 8 == 0:
         return _SwiGLU.apply(a, b)
     return F.silu(a) * b
+
+
+class _CrossEntropy(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, logits, targets):
+        loss_rows, lse = _ext.load().cross_entropy_fwd(logits, targets)
+        ctx.save_for_backward(logits, targets, lse)
+        return loss_rows.mean()
+
+    @staticmethod
+    def backward(ctx, g):
+        logits, targets, lse = ctx.saved_tensors
+        # the upstream scalar is read by the kernel on the device: no host sync
+        gs = g.reshape(1).to(torch.float32).contiguous()
+        return _ext.load().cross_entropy_bwd(logits, targets, lse, 1.0 / logits.shape[0], gs), None
+
+
+def cross_entropy(logits: Tensor, targets: Tensor) -> Tensor:
+    """Mean next-token cross entropy; fp32 math, bf16 logits read once per pass on CUDA."""
+    flat = logits.reshape(-1, logits.shape[-1])
+    t = targets.reshape(-1)
+    if _native(flat) and flat.shape[-1] % 8 == 0 and t.dtype == torch.int64:
+        return _CrossEntropy.apply(flat.contiguous(), t.contiguous())
+    return F.cross_entropy(flat.float(), t)

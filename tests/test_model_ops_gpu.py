@@ -40,3 +40,17 @@ def test_swiglu_fwd_bwd():
     hr.backward(g)
     torch.testing.assert_close(a.grad.float(), ar.grad, rtol=2e-2, atol=3e-2)
     torch.testing.assert_close(b.grad.float(), br.grad, rtol=2e-2, atol=3e-2)
+
+
+@pytest.mark.parametrize("T,V", [(64, 1024), (33, 32000), (8, 128256)])
+def test_cross_entropy_fwd_bwd(T, V):
+    torch.manual_seed(2)
+    logits = (torch.randn(T, V, device="cuda") * 3).bfloat16().requires_grad_()
+    targets = torch.randint(0, V, (T,), device="cuda")
+    ref_in = logits.detach().float().requires_grad_()
+    loss = model_ops.cross_entropy(logits, targets)
+    ref = F.cross_entropy(ref_in, targets)
+    torch.testing.assert_close(loss, ref, rtol=1e-4, atol=1e-4)
+    loss.backward()
+    ref.backward()
+    torch.testing.assert_close(logits.grad.float(), ref_in.grad, rtol=2e-2, atol=1e-4)
