@@ -124,7 +124,7 @@ def build_ours(args, world, device):
     from dtensor_muon_b200.optim import Muon
     from dtensor_muon_b200.train import build_llama, build_optimizer
 
-    cfg = preset(args.model, max_seq_len=args.seq)
+    cfg = preset(args.model, max_seq_len=args.seq, **({"n_layers": args.layers} if args.layers else {}))
     mesh = None
     if world > 1:
         from torch.distributed.device_mesh import init_device_mesh
@@ -235,6 +235,7 @@ def parse_args():
     ap.add_argument("--lr", type=float, default=1e-3)
     ap.add_argument("--strategy", default="polar_express")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--layers", type=int, default=0, help="diagnostics only: override the layer count")
     ap.add_argument("--fuse-momentum", type=int, default=int(os.environ.get("DMB_FUSE_MOMENTUM", "0")),
                     help="ours, N > 1: Muon momentum update inside the FSDP gradient reduce-scatter")
     ap.add_argument("--fsdp-comm", default=os.environ.get("DMB_FSDP_COMM", "p2p"), choices=["p2p", "nccl"],
