@@ -33,8 +33,6 @@ _LAUNCHES = {
     "dist_pack": 2,
     "dist_apply": 1,
     "dist_barrier": 1,
-    "fsdp_all_gather_pull": 1,
-    "fsdp_reduce_scatter_pull": 1,
     "push_slots": 1,
     "local_slot_sum": 1,
     "rs_sum_momentum": 1,

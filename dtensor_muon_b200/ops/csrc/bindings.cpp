@@ -59,16 +59,13 @@ void dist_pack(const at::Tensor& meta_i64, const at::Tensor& meta_i32, const at:
 void dist_apply(const at::Tensor& meta_i64, const at::Tensor& meta_i32, const at::Tensor& peer_base,
                 std::vector<int64_t> ints, std::vector<double> floats, bool has_var);
 void dist_barrier(const at::Tensor& flag_base, int64_t rank, int64_t world, int64_t epoch);
-void fsdp_all_gather_pull(at::Tensor& out, const at::Tensor& peer_base, int64_t off, int64_t in_bytes, int64_t world,
-                          int64_t max_ctas);
 void push_slots(const at::Tensor& src, const at::Tensor& peer_base, int64_t off, int64_t slot_bytes, int64_t rank,
                 int64_t world, bool per_peer, int64_t max_ctas);
 void local_slot_sum(at::Tensor& out, const at::Tensor& staging_bytes, int64_t off, int64_t world, double scale,
                     int64_t max_ctas);
 void rs_sum_momentum(at::Tensor& out, const at::Tensor& staging_bytes, int64_t off, int64_t world, double scale,
                      const at::Tensor& segs, int64_t max_ctas);
-void fsdp_reduce_scatter_pull(at::Tensor& out, const at::Tensor& peer_base, int64_t off, int64_t rank, int64_t world,
-                              double scale, int64_t max_ctas);
+
 
 // ---- ep_ops.cu
 void ep_scatter_rows(const at::Tensor& src, const at::Tensor& dst_rank, const at::Tensor& dst_row,
@@ -135,8 +132,6 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("dist_pack", &dmb::dist_pack);
   m.def("dist_apply", &dmb::dist_apply);
   m.def("dist_barrier", &dmb::dist_barrier);
-  m.def("fsdp_all_gather_pull", &dmb::fsdp_all_gather_pull);
-  m.def("fsdp_reduce_scatter_pull", &dmb::fsdp_reduce_scatter_pull);
   m.def("push_slots", &dmb::push_slots);
   m.def("local_slot_sum", &dmb::local_slot_sum);
   m.def("rs_sum_momentum", &dmb::rs_sum_momentum);

@@ -503,108 +503,7 @@ void dist_barrier(const at::Tensor& flag_base, int64_t rank, int64_t world, int6
 
 // ------------------------------------------------------------------------
 // FSDP collectives over peer memory (plugged into FSDP2 through its custom
-// all-gather / reduce-scatter hooks). Each rank's input is first staged in its
-// symmetric buffer; after a barrier every rank pulls what it needs.
-namespace dmb {
-namespace {
-
-// out[k * n + i] = staging_k[i] for every rank k (16-byte vectors). Each
-// thread keeps UNROLL independent loads in flight to cover NVLink latency.
-constexpr int AG_UNROLL = 4;
-__global__ void ag_pull_kernel(uint4* __restrict__ out, const int64_t* peer_base, long long off, long long n_vec,
-                               int world) {
-  const long long total = n_vec * world;
-  const long long stride = (long long)gridDim.x * blockDim.x;
-  for (long long i0 = (long long)blockIdx.x * blockDim.x + threadIdx.x; i0 < total; i0 += stride * AG_UNROLL) {
-    uint4 v[AG_UNROLL];
-#pragma unroll
-    for (int u = 0; u < AG_UNROLL; ++u) {
-      const long long i = i0 + u * stride;
-      if (i < total) {
-        const int k = (int)(i / n_vec);
-        v[u] = reinterpret_cast<const uint4*>(peer_base[k] + off)[i - (long long)k * n_vec];
-      }
-    }
-#pragma unroll
-    for (int u = 0; u < AG_UNROLL; ++u) {
-      const long long i = i0 + u * stride;
-      if (i < total) out[i] = v[u];
-    }
-  }
-}
-
-// out[i] = scale * sum_k staging_k[rank * n + i], fp32 accumulation; dt 0 fp32 / 1 bf16.
-// All peers' loads for a vector are issued before any is consumed.
-constexpr int RS_MAX_WORLD = 8;
-__global__ void rs_pull_kernel(void* __restrict__ out, const int64_t* peer_base, long long off, long long n, int rank,
-                               int world, int dt, float scale) {
-  const long long n8 = n / 8;
-  for (long long v = (long long)blockIdx.x * blockDim.x + threadIdx.x; v < n8; v += (long long)gridDim.x * blockDim.x) {
-    float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-    const long long idx = (long long)rank * n + v * 8;
-    if (dt == 1 && world <= RS_MAX_WORLD) {
-      uint4 raw[RS_MAX_WORLD];
-#pragma unroll
-      for (int k = 0; k < RS_MAX_WORLD; ++k)
-        if (k < world)
-          raw[k] = *reinterpret_cast<const uint4*>(reinterpret_cast<const __nv_bfloat16*>(peer_base[k] + off) + idx);
-#pragma unroll
-      for (int k = 0; k < RS_MAX_WORLD; ++k) {
-        if (k < world) {
-          const uint32_t w[4] = {raw[k].x, raw[k].y, raw[k].z, raw[k].w};
-#pragma unroll
-          for (int e = 0; e < 4; ++e) {
-            acc[2 * e] += bf16_bits_to_float((uint16_t)(w[e] & 0xFFFFu));
-            acc[2 * e + 1] += bf16_bits_to_float((uint16_t)(w[e] >> 16));
-          }
-        }
-      }
-    } else {
-      for (int k = 0; k < world; ++k) {
-        float x[8];
-        load8(reinterpret_cast<const void*>(peer_base[k] + off), dt, idx, x);
-#pragma unroll
-        for (int e = 0; e < 8; ++e) acc[e] += x[e];
-      }
-    }
-#pragma unroll
-    for (int e = 0; e < 8; ++e) acc[e] *= scale;
-    store8(out, dt, v * 8, acc);
-  }
-}
-
-}  // namespace
-
-void fsdp_all_gather_pull(at::Tensor& out, const at::Tensor& peer_base, int64_t off, int64_t in_bytes, int64_t world,
-                          int64_t max_ctas) {
-  const at::cuda::CUDAGuard guard(out.device());
-  TORCH_CHECK(in_bytes % 16 == 0 && off % 16 == 0 && out.is_contiguous());
-  TORCH_CHECK(out.numel() * out.element_size() == in_bytes * world);
-  const long long n_vec = in_bytes / 16;
-  if (n_vec == 0) return;
-  const int blocks = (int)std::min<long long>(max_ctas, (n_vec * world + 255) / 256);
-  ag_pull_kernel<<<blocks, 256, 0, at::cuda::getCurrentCUDAStream()>>>(reinterpret_cast<uint4*>(out.data_ptr()),
-                                                                       peer_base.data_ptr<int64_t>(), off, n_vec,
-                                                                       (int)world);
-  C10_CUDA_KERNEL_LAUNCH_CHECK();
-}
-
-void fsdp_reduce_scatter_pull(at::Tensor& out, const at::Tensor& peer_base, int64_t off, int64_t rank, int64_t world,
-                              double scale, int64_t max_ctas) {
-  const at::cuda::CUDAGuard guard(out.device());
-  TORCH_CHECK(out.is_contiguous() && (out.scalar_type() == at::kFloat || out.scalar_type() == at::kBFloat16));
-  const long long n = out.numel();
-  TORCH_CHECK(n % 8 == 0 && off % 16 == 0);
-  if (n == 0) return;
-  const int blocks = (int)std::min<long long>(max_ctas, (n / 8 + 255) / 256);
-  rs_pull_kernel<<<blocks, 256, 0, at::cuda::getCurrentCUDAStream()>>>(
-      out.data_ptr(), peer_base.data_ptr<int64_t>(), off, n, (int)rank, (int)world,
-      out.scalar_type() == at::kFloat ? 0 : 1, (float)scale);
-  C10_CUDA_KERNEL_LAUNCH_CHECK();
-}
-
-}  // namespace dmb
-
+// all-gather / reduce-scatter hooks, parallel/fsdp_comm.py).
 // ---- push variants: stores into peers' staging (one barrier per collective)
 namespace dmb {
 namespace {
