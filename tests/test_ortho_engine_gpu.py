@@ -114,3 +114,51 @@ def test_orthogonalize_2sm_matches_1sm(strategy):
         C.set_gemm_variant(prev)
     assert _close_frac(two, one, rtol=1e-2, atol=3e-2) < 0.01
     _ext.check_device_errors("cuda")
+
+
+# ---- contracts, determinism, degenerate inputs (mirrors tests/kernels/test_gram.py) ----
+def test_orthogonalize_is_deterministic():
+    torch.manual_seed(8)
+    g = list(torch.randn(3, 300, 700, device="cuda").unbind(0))
+    a = torch.stack(ortho.orthogonalize_native(g, 5, "polar_express"))
+    b = torch.stack(ortho.orthogonalize_native(g, 5, "polar_express"))
+    assert torch.equal(a, b)
+    x = torch.randn(2, 512, 1024, device="cuda").bfloat16()
+    assert torch.equal(ortho.gram(x), ortho.gram(x))
+
+
+def test_non_contiguous_and_transposed_inputs():
+    from dtensor_muon_b200.orthogonalize import foreach_zeropower, zeropower
+
+    torch.manual_seed(9)
+    base = torch.randn(2, 512, 384, device="cuda")
+    views = [base[i].mT for i in range(2)]  # non-contiguous [384, 512]
+    got = foreach_zeropower(views, steps=5, strategy="newton_schulz")
+    ref = foreach_zeropower([v.contiguous() for v in views], steps=5, strategy="newton_schulz")
+    for a, b in zip(got, ref):
+        assert a.shape == (384, 512) and torch.equal(a, b)
+    one = zeropower(base[0][:, ::2], steps=5)  # strided columns
+    assert one.shape == (512, 192) and torch.isfinite(one.float()).all()
+
+
+def test_zero_and_rank_one_inputs_stay_finite():
+    z = torch.zeros(2, 256, 512, device="cuda")
+    out = torch.stack(ortho.orthogonalize_native(list(z.unbind(0)), 5, "polar_express"))
+    assert torch.isfinite(out.float()).all() and out.abs().max() == 0
+    r = torch.randn(256, 1, device="cuda") @ torch.randn(1, 512, device="cuda")
+    out = ortho.orthogonalize_native([r], 5, "newton_schulz")[0]
+    assert torch.isfinite(out.float()).all()
+    assert ortho.orthogonalize_native([], 5, "newton_schulz") == []
+
+
+def test_engine_contracts_raise():
+    C = _ext.load()
+    x = torch.randn(1, 256, 256, device="cuda")  # fp32: not accepted by the GEMM
+    out = torch.empty(1, 256, 256, device="cuda", dtype=torch.bfloat16)
+    with pytest.raises(RuntimeError):
+        C.gram_sym(x, out, None, None, 1.0, 0.0, 0, 0, 0)
+    xb = torch.randn(1, 200, 256, device="cuda").bfloat16()  # rows not a multiple of 256
+    with pytest.raises(RuntimeError, match="multiples of 256"):
+        C.gram_sym2(xb, out, None, None, 1.0, 0.0, 0, 0)
+    with pytest.raises(AssertionError, match="only supports up to 5"):
+        ortho.orthogonalize_native([torch.randn(8, 8, device="cuda")], 6, "polar_express")
