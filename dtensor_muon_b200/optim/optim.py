@@ -457,6 +457,12 @@ class Muon(torch.optim.Optimizer):
         state_lists: dict[str, list[Tensor]] = {k: [] for k in algorithm.state_spec}
         self._init_muon_group(group, algorithm, params, grads, state_lists, lr_ratios, steps)
         impl = self._raw_muon_impl(algorithm) if torch.compiler.is_compiling() else self._get_muon_impl(algorithm)
+        from ..parallel.owner_compute import deferred
+
+        with deferred():  # owner-compute batches of this group run phase by phase at exit
+            self._call_impl(impl, group, algorithm, params, grads, state_lists, lr_ratios)
+
+    def _call_impl(self, impl, group, algorithm, params, grads, state_lists, lr_ratios) -> None:
         impl(
             params,
             grads,

@@ -10,7 +10,8 @@ result back (P2P loads inside the apply kernel). Sequence per batch:
     barrier | dist_pack (+ sums push) | barrier | owner: finalize + ortho [+ NorMuon] | barrier | dist_apply
 
 Matrices are assigned in contiguous chunks (matrix b -> rank b // ceil(B/W)),
-like a Shard(0) of the stacked batch.
+like a Shard(0) of the stacked batch. Inside :class:`deferred` (the Muon step
+uses it) all batches of the step run phase by phase with three barriers in total.
 """
 
 from __future__ import annotations
@@ -105,80 +106,157 @@ def owner_compute_update(
     order: dict[float, list[int]] = {}
     for i, lr in enumerate(lr_effs):
         order.setdefault(float(lr), []).append(i)
+    specs = []
     for lr_eff, idxs in order.items():
         step = world * max_slots
         for s in range(0, len(idxs), step):
-            sel = idxs[s : s + step]
-            _run_batch(
-                C_, ws, sel, params, grads, buffers, variances, lr_eff, lay, R, C, r0, r1, g1, rank, world,
-                coeffs, fac, eps, weight_decay, cautious_wd, momentum, nesterov, maximize, muon_beta2, has_var,
-                device, momentum_done,
-            )
+            specs.append(_Spec(
+                C_, ws, idxs[s : s + step], params, grads, buffers, variances, lr_eff, lay, R, C, r0, r1, g1, rank,
+                world, coeffs, fac, eps, weight_decay, cautious_wd, momentum, nesterov, maximize, muon_beta2,
+                has_var, device, momentum_done,
+            ))
+    if _DEFER.get("on"):
+        pend = _DEFER.setdefault("pending", {}).setdefault(id(ws), (ws, []))[1]
+        pend.extend(specs)
+        if sum(sp.nbytes for sp in pend) > MAX_DEFERRED_BYTES:
+            flush(ws)
+        return
+    for sp in specs:
+        _run_phases(ws, [sp])
 
 
-def _run_batch(C_, ws, sel, params, grads, buffers, variances, lr_eff, lay, R, C, r0, r1, g1, rank, world, coeffs,
-               fac, eps, weight_decay, cautious_wd, momentum, nesterov, maximize, muon_beta2, has_var, device,
-               momentum_done=False):
-    S = len(sel)
-    Bo = math.ceil(S / world)
-    steps = coeffs.shape[0]
-    # Symmetric layout: sums | vbuf | rowscale | x | x2
-    sums_off = 0
-    vbuf_off = _align(sums_off + Bo * world * 4)
-    rs_off = _align(vbuf_off + (Bo * R * 4 if has_var else 0))
-    x_off = _align(rs_off + (Bo * R * 4 if has_var else 0))
-    slot_bytes = lay.Np * lay.Mp * 2
-    x2_off = _align(x_off + Bo * slot_bytes)
-    total = x2_off + Bo * slot_bytes
-    buf, peer_base = ws.buffer(total)
-    res_off = x_off if steps % 2 == 0 else x2_off
+# Deferred execution: inside ``deferred()`` every owner-compute batch of the
+# optimizer step is queued; at exit all batches share one symmetric buffer and
+# run phase by phase (all packs | barrier | all owner GEMMs | barrier | all
+# applies), so the step pays three barriers instead of three per batch and the
+# packs' NVLink traffic drains together.
+_DEFER: dict = {}
+MAX_DEFERRED_BYTES = 32 << 30
 
-    loc = lambda t: t.to_local()  # noqa: E731
-    ptrs = [
-        [loc(grads[i]).data_ptr() for i in sel],
-        [loc(buffers[i]).data_ptr() for i in sel],
-        [loc(params[i]).data_ptr() for i in sel],
-        [loc(variances[i]).data_ptr() for i in sel] if has_var else [0] * S,
-    ]
-    meta64 = torch.tensor(ptrs, dtype=torch.int64).pin_memory().to(device, non_blocking=True)
-    owner = [b // Bo for b in range(S)]
-    slot = [b % Bo for b in range(S)]
-    meta32 = torch.tensor([owner, slot], dtype=torch.int32).pin_memory().to(device, non_blocking=True)
-    ints = [
-        x_off, res_off, sums_off, vbuf_off, rs_off,
-        dtype_code(grads[sel[0]].dtype), dtype_code(params[sel[0]].dtype),
-        R, C, int(lay.transpose), lay.Np, lay.Mp, r0, r1, g1, rank, world,
-        int(nesterov), 0 if momentum_done else int(maximize), int(cautious_wd), int(has_var),
-        int(all(x % 16 == 0 for row in ptrs[:3] for x in row)),
-    ]
-    floats = [float(momentum), float(lr_eff), float(weight_decay)]
 
-    with nvtx("dmb.owner.pack"):
-        ws.barrier()  # every reader of the previous batch's results is done
-        C_.dist_pack(meta64, meta32, peer_base, ints, floats, not momentum_done, has_var)
-        ws.barrier()  # all shards have landed in the owners' workspaces
+class deferred:
+    def __enter__(self):
+        self._prev = _DEFER.get("on", False)
+        _DEFER["on"] = True
+        return self
 
-    mine = max(0, min(Bo, S - rank * Bo))
-    if mine > 0:
+    def __exit__(self, exc_type, exc, tb):
+        _DEFER["on"] = self._prev
+        pending = _DEFER.pop("pending", {}) if not self._prev else {}
+        if exc_type is None:
+            for ws, specs in pending.values():
+                if specs:
+                    _run_phases(ws, specs)
+        return False
+
+
+def flush(ws) -> None:
+    pend = _DEFER.get("pending", {}).pop(id(ws), None)
+    if pend and pend[1]:
+        _run_phases(pend[0], pend[1])
+
+
+class _Spec:
+    """One owner-compute batch: pointer tables, symmetric-buffer layout, kernel arguments."""
+
+    def __init__(self, C_, ws, sel, params, grads, buffers, variances, lr_eff, lay, R, C, r0, r1, g1, rank, world,
+                 coeffs, fac, eps, weight_decay, cautious_wd, momentum, nesterov, maximize, muon_beta2, has_var,
+                 device, momentum_done):
+        self.C_, self.lay, self.R, self.C, self.coeffs, self.fac, self.eps = C_, lay, R, C, coeffs, fac, eps
+        self.has_var, self.device, self.muon_beta2, self.momentum_done = has_var, device, muon_beta2, momentum_done
+        S = len(sel)
+        self.Bo = Bo = math.ceil(S / world)
+        self.world, self.rank = world, rank
+        self.mine = max(0, min(Bo, S - rank * Bo))
+        self.slot_bytes = lay.Np * lay.Mp * 2
+        # Layout relative to this batch's base: sums | vbuf | rowscale | x | x2
+        self.sums_rel = 0
+        self.vbuf_rel = _align(Bo * world * 4)
+        self.rs_rel = _align(self.vbuf_rel + (Bo * R * 4 if has_var else 0))
+        self.x_rel = _align(self.rs_rel + (Bo * R * 4 if has_var else 0))
+        self.x2_rel = _align(self.x_rel + Bo * self.slot_bytes)
+        self.nbytes = _align(self.x2_rel + Bo * self.slot_bytes)
+        loc = lambda t: t.to_local()  # noqa: E731
+        self.ptrs = [
+            [loc(grads[i]).data_ptr() for i in sel],
+            [loc(buffers[i]).data_ptr() for i in sel],
+            [loc(params[i]).data_ptr() for i in sel],
+            [loc(variances[i]).data_ptr() for i in sel] if has_var else [0] * S,
+        ]
+        self.meta64 = torch.tensor(self.ptrs, dtype=torch.int64).pin_memory().to(device, non_blocking=True)
+        owner = [b // Bo for b in range(S)]
+        slot = [b % Bo for b in range(S)]
+        self.meta32 = torch.tensor([owner, slot], dtype=torch.int32).pin_memory().to(device, non_blocking=True)
+        self.gdt, self.pdt = dtype_code(grads[sel[0]].dtype), dtype_code(params[sel[0]].dtype)
+        self.geom = (r0, r1, g1)
+        self.flags = (int(nesterov), 0 if momentum_done else int(maximize), int(cautious_wd))
+        self.floats = [float(momentum), float(lr_eff), float(weight_decay)]
+        self.vec_ok = int(all(x % 16 == 0 for row in self.ptrs[:3] for x in row))
+
+    def place(self, base: int) -> None:
+        self.base = base
+        steps = self.coeffs.shape[0]
+        x_off, x2_off = base + self.x_rel, base + self.x2_rel
+        res_off = x_off if steps % 2 == 0 else x2_off
+        r0, r1, g1 = self.geom
+        lay = self.lay
+        self.ints = [
+            x_off, res_off, base + self.sums_rel, base + self.vbuf_rel, base + self.rs_rel,
+            self.gdt, self.pdt, self.R, self.C, int(lay.transpose), lay.Np, lay.Mp, r0, r1, g1, self.rank,
+            self.world, self.flags[0], self.flags[1], self.flags[2], int(self.has_var), self.vec_ok,
+        ]
+
+    def pack(self, peer_base):
+        self.C_.dist_pack(self.meta64, self.meta32, peer_base, self.ints, self.floats, not self.momentum_done,
+                          self.has_var)
+
+    def compute(self, buf):
+        if self.mine == 0:
+            return
+        C_, lay, mine, base = self.C_, self.lay, self.mine, self.base
+
         def region(off, n, dtype, shape):
-            return buf[off : off + n].view(dtype).view(shape)
+            return buf[base + off : base + off + n].view(dtype).view(shape)
 
-        x = region(x_off, mine * slot_bytes, torch.bfloat16, (mine, lay.Np, lay.Mp))
-        x2 = region(x2_off, mine * slot_bytes, torch.bfloat16, (mine, lay.Np, lay.Mp))
-        sums = region(sums_off, Bo * world * 4, torch.float32, (Bo, world))[:mine].contiguous()
-        inv = C_.norm_finalize(sums, fac, eps)
-        a_ws = WORKSPACE.get(device, "a", (mine, lay.Np, lay.Np))
-        b_ws = WORKSPACE.get(device, "b", (mine, lay.Np, lay.Np))
-        res = C_.ortho_iterate(x, x2, a_ws, b_ws, inv, coeffs, 0)
-        if has_var:
-            rowsq = C_.row_sumsq(res, lay.transpose, R, C)
-            vbase = buf.data_ptr() + vbuf_off
+        x = region(self.x_rel, mine * self.slot_bytes, torch.bfloat16, (mine, lay.Np, lay.Mp))
+        x2 = region(self.x2_rel, mine * self.slot_bytes, torch.bfloat16, (mine, lay.Np, lay.Mp))
+        sums = region(self.sums_rel, self.Bo * self.world * 4, torch.float32, (self.Bo, self.world))[:mine]
+        inv = C_.norm_finalize(sums.contiguous(), self.fac, self.eps)
+        a_ws = WORKSPACE.get(self.device, "a", (mine, lay.Np, lay.Np))
+        b_ws = WORKSPACE.get(self.device, "b", (mine, lay.Np, lay.Np))
+        res = C_.ortho_iterate(x, x2, a_ws, b_ws, inv, self.coeffs, 0)
+        if self.has_var:
+            R = self.R
+            rowsq = C_.row_sumsq(res, lay.transpose, R, self.C)
+            vbase = buf.data_ptr() + base + self.vbuf_rel
             vptrs = torch.tensor([vbase + s * R * 4 for s in range(mine)], dtype=torch.int64).pin_memory()
-            rowscale = C_.normuon_finalize(rowsq, vptrs.to(device, non_blocking=True), C, muon_beta2)
-            region(rs_off, mine * R * 4, torch.float32, (mine, R)).copy_(rowscale)
+            rowscale = C_.normuon_finalize(rowsq, vptrs.to(self.device, non_blocking=True), self.C, self.muon_beta2)
+            region(self.rs_rel, mine * R * 4, torch.float32, (mine, R)).copy_(rowscale)
+
+    def apply(self, peer_base):
+        self.C_.dist_apply(self.meta64, self.meta32, peer_base, self.ints, self.floats, self.has_var)
+
+
+def _run_phases(ws, specs: list) -> None:
+    total, base = 0, []
+    for sp in specs:
+        base.append(total)
+        total += sp.nbytes
+    buf, peer_base = ws.buffer(total)
+    for sp, b in zip(specs, base):
+        sp.place(b)
+    with nvtx("dmb.owner.pack"):
+        ws.barrier()  # every reader of the previous step's results is done
+        for sp in specs:
+            sp.pack(peer_base)
+        ws.barrier()  # all shards have landed in the owners' workspaces
+    with nvtx("dmb.owner.compute"):
+        for sp in specs:
+            sp.compute(buf)
     with nvtx("dmb.owner.apply"):
         ws.barrier()  # owners' results are ready
-        C_.dist_apply(meta64, meta32, peer_base, ints, floats, has_var)
+        for sp in specs:
+            sp.apply(peer_base)
 
 
 def fsdp3d_local_eligible(params, grads, buffers) -> bool:
