@@ -115,14 +115,7 @@ def owner_compute_update(
                 world, coeffs, fac, eps, weight_decay, cautious_wd, momentum, nesterov, maximize, muon_beta2,
                 has_var, device, momentum_done,
             ))
-    if _DEFER.get("on"):
-        pend = _DEFER.setdefault("pending", {}).setdefault(id(ws), (ws, []))[1]
-        pend.extend(specs)
-        if sum(sp.nbytes for sp in pend) > MAX_DEFERRED_BYTES:
-            flush(ws)
-        return
-    for sp in specs:
-        _run_phases(ws, [sp])
+    _enqueue(ws, specs)
 
 
 # Deferred execution: inside ``deferred()`` every owner-compute batch of the
@@ -148,6 +141,19 @@ class deferred:
                 if specs:
                     _run_phases(ws, specs)
         return False
+
+
+def _enqueue(ws, specs: list) -> None:
+    """Queue ``specs`` inside :class:`deferred` (flushing once the queue exceeds
+    ``MAX_DEFERRED_BYTES``); outside it, run each batch at once."""
+    if _DEFER.get("on"):
+        pend = _DEFER.setdefault("pending", {}).setdefault(id(ws), (ws, []))[1]
+        pend.extend(specs)
+        if sum(sp.nbytes for sp in pend) > MAX_DEFERRED_BYTES:
+            flush(ws)
+        return
+    for sp in specs:
+        _run_phases(ws, [sp])
 
 
 def flush(ws) -> None:
