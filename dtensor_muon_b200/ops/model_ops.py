@@ -1,7 +1,8 @@
-"""Autograd wrappers for the fused decoder-block kernels (``ops/csrc/model_ops.cu``).
+"""Entry points for the fused decoder-block kernels (``ops/csrc/model_ops.cu``).
 
-``rope`` and ``swiglu`` run the native kernels for contiguous bf16 CUDA inputs
-and the equivalent PyTorch composition otherwise (CPU, fp32).
+``rope``, ``swiglu`` and ``cross_entropy`` run the native kernels, registered
+as ``torch.library`` ops with their autograd formulas (``ops/library.py``), for
+bf16 CUDA inputs and the equivalent PyTorch composition otherwise (CPU, fp32).
 """
 
 from __future__ import annotations
@@ -10,7 +11,7 @@ import torch
 import torch.nn.functional as F
 from torch import Tensor
 
-from . import _ext
+from . import _ext, library
 
 
 def _native(*ts: Tensor) -> bool:
@@ -26,58 +27,17 @@ def rope_reference(x: Tensor, cos: Tensor, sin: Tensor) -> Tensor:
     return torch.stack((x0 * c - x1 * s, x0 * s + x1 * c), dim=-1).flatten(-2).to(x.dtype)
 
 
-class _Rope(torch.autograd.Function):
-    @staticmethod
-    def forward(ctx, x, cos, sin):
-        ctx.save_for_backward(cos, sin)
-        return _ext.load().rope(x.contiguous(), cos, sin, 1.0)
-
-    @staticmethod
-    def backward(ctx, g):
-        cos, sin = ctx.saved_tensors
-        return _ext.load().rope(g.contiguous(), cos, sin, -1.0), None, None
-
-
 def rope(x: Tensor, cos: Tensor, sin: Tensor) -> Tensor:
     if _native(x) and x.shape[-1] % 8 == 0:
-        return _Rope.apply(x, cos.contiguous(), sin.contiguous())
+        return library.rope(x, cos, sin, 1.0)
     return rope_reference(x, cos, sin)
-
-
-class _SwiGLU(torch.autograd.Function):
-    @staticmethod
-    def forward(ctx, a, b):
-        a, b = a.contiguous(), b.contiguous()
-        ctx.save_for_backward(a, b)
-        return _ext.load().swiglu_fwd(a, b)
-
-    @staticmethod
-    def backward(ctx, g):
-        a, b = ctx.saved_tensors
-        da, db = _ext.load().swiglu_bwd(a, b, g.contiguous())
-        return da, db
 
 
 def swiglu(a: Tensor, b: Tensor) -> Tensor:
     """silu(a) * b."""
     if _native(a, b) and a.numel() % 8 == 0:
-        return _SwiGLU.apply(a, b)
+        return library.swiglu(a, b)
     return F.silu(a) * b
-
-
-class _CrossEntropy(torch.autograd.Function):
-    @staticmethod
-    def forward(ctx, logits, targets):
-        loss_rows, lse = _ext.load().cross_entropy_fwd(logits, targets)
-        ctx.save_for_backward(logits, targets, lse)
-        return loss_rows.mean()
-
-    @staticmethod
-    def backward(ctx, g):
-        logits, targets, lse = ctx.saved_tensors
-        # the upstream scalar is read by the kernel on the device: no host sync
-        gs = g.reshape(1).to(torch.float32).contiguous()
-        return _ext.load().cross_entropy_bwd(logits, targets, lse, 1.0 / logits.shape[0], gs), None
 
 
 def cross_entropy(logits: Tensor, targets: Tensor) -> Tensor:
@@ -85,5 +45,5 @@ def cross_entropy(logits: Tensor, targets: Tensor) -> Tensor:
     flat = logits.reshape(-1, logits.shape[-1])
     t = targets.reshape(-1)
     if _native(flat) and flat.shape[-1] % 8 == 0 and t.dtype == torch.int64:
-        return _CrossEntropy.apply(flat.contiguous(), t.contiguous())
+        return library.cross_entropy(flat, t)[0]
     return F.cross_entropy(flat.float(), t)
