@@ -1,7 +1,7 @@
 """Small single-kernel cases for ncu captures (one GPU, a few launches, inputs
 larger than L2 but a few GB at most).
 
-    python benchmarks/ncu_cases.py --case pack|apply|adamw|lp|rope|swiglu|gemm2_gram|gemm2_bx
+    python benchmarks/ncu_cases.py --case pack|apply|adamw|lp|rope|swiglu|gemm2_gram|gemm2_bx|pe_64x1024
 """
 
 from __future__ import annotations
@@ -83,6 +83,13 @@ def main():
                 C.gram_sym2(x, a, None, None, 1.0, 0.0, 0, 0)
             else:
                 C.gemm_ax2(a, x, out, x, None, 1.0, 0.5, 0, 0)
+    elif case == "pe_64x1024":
+        # short-K case: PE-5 on 64 x 1024 x 1024 through the public engine entry (18 launches per call)
+        from dtensor_muon_b200.ops import ortho
+
+        mats = list(torch.randn(64, 1024, 1024, device=dev).bfloat16().unbind(0))
+        for _ in range(8):
+            ortho.orthogonalize_native(mats, 5, "polar_express")
     else:
         raise SystemExit(f"unknown case {case}")
     torch.cuda.synchronize()
