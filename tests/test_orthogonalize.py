@@ -181,3 +181,55 @@ def _mesh2d_worker(rank, world):
 
 def test_dtensor_2d_mesh_gloo_four_ranks():
     run_distributed(_mesh2d_worker, 4)
+
+
+def test_ns_coefficient_override_changes_the_iteration():
+    torch.manual_seed(3)
+    g = torch.randn(16, 24)
+    default = ns_loop(g.bfloat16(), 5)
+    same = ns_loop(g.bfloat16(), 5, a=3.4445, b=-4.7750, c=2.0315)
+    cubic = ns_loop(g.bfloat16(), 5, a=1.5, b=-0.5, c=0.0)  # classic cubic Newton-Schulz
+    torch.testing.assert_close(default, same)
+    assert not torch.equal(default, cubic)
+    # the cubic iteration converges monotonically towards singular values 1 from below
+    sv = _sv(ns_loop(g.bfloat16(), 12, a=1.5, b=-0.5, c=0.0).float())
+    assert float(sv.max()) < 1.05 and float(sv.min()) > 0.0
+
+
+@pytest.mark.parametrize("strategy", list(LOOPS))
+def test_rank_deficient_input_stays_finite(strategy):
+    torch.manual_seed(4)
+    u = torch.randn(32, 3)
+    v = torch.randn(3, 48)
+    g = u @ v  # rank 3
+    out = zeropower(g, steps=5, strategy=strategy, use_native=False)
+    assert torch.isfinite(out.float()).all()
+    sv = _sv(out.float())
+    # the 3 directions of the input are kept (the bf16 rounding noise in the
+    # null space is amplified too, so only the top of the spectrum is checked)
+    assert float(sv[:3].min()) > 0.5 and float(sv.max()) < 1.3
+
+
+def _foreach_sign_worker(rank, world):
+    import torch
+    from torch.distributed.device_mesh import init_device_mesh
+    from torch.distributed.tensor import Replicate, Shard, distribute_tensor
+
+    import dtensor_muon_b200.optim.optim  # noqa: F401  (registers the strategy)
+
+    mesh = init_device_mesh("cpu", (world,))
+    torch.manual_seed(5)
+    fulls = [torch.randn(6, 4), torch.randn(5, 3), torch.randn(4, 4)]
+    ds = [
+        distribute_tensor(fulls[0], mesh, [Shard(0)]),
+        distribute_tensor(fulls[1], mesh, [Shard(1)]),
+        distribute_tensor(fulls[2], mesh, [Replicate()]),
+    ]
+    torch._foreach_sign_(ds)
+    for d, f, pl in zip(ds, fulls, ([Shard(0)], [Shard(1)], [Replicate()])):
+        assert list(d.placements) == pl
+        torch.testing.assert_close(d.full_tensor(), f.sign())
+
+
+def test_dtensor_foreach_sign_strategy_gloo():
+    run_distributed(_foreach_sign_worker, 2)
