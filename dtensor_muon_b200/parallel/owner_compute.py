@@ -17,6 +17,7 @@ uses it) all batches of the step run phase by phase with three barriers in total
 from __future__ import annotations
 
 import math
+from dataclasses import dataclass
 
 import torch
 from torch import Tensor
@@ -86,35 +87,33 @@ def owner_compute_update(
 ) -> None:
     """``momentum_done``: the grads already hold g' (momentum updated in the
     FSDP reduce-scatter), so the pack only casts and scatters them."""
-    C_ = _ext.load()
-    coeffs = coefficient_table(strategy, ns_steps)
     mesh = grads[0].device_mesh
-    group = mesh.get_group()
     world, rank = mesh.size(), mesh.get_local_rank()
     R, C = grads[0].shape
     lay = layout_for(R, C)
     r0, r1 = _rows(R, world, rank)
-    g1 = (lay.Mp if lay.transpose else lay.Np) if rank == world - 1 else r1
     device = grads[0].to_local().device
-    ws = symm.workspace_for(group, device)
-    fac = norm_factor(strategy)
-    has_var = variances is not None
+    ws = symm.workspace_for(mesh.get_group(), device)
+    grp = _Group(
+        C_=_ext.load(), lay=lay, R=R, C=C, rank=rank, world=world, r0=r0, r1=r1,
+        g1=(lay.Mp if lay.transpose else lay.Np) if rank == world - 1 else r1,
+        coeffs=coefficient_table(strategy, ns_steps), fac=norm_factor(strategy), eps=eps,
+        weight_decay=weight_decay, cautious_wd=cautious_wd, momentum=momentum, nesterov=nesterov,
+        maximize=maximize, muon_beta2=muon_beta2, has_var=variances is not None, device=device,
+        momentum_done=momentum_done, gdt=dtype_code(grads[0].dtype), pdt=dtype_code(params[0].dtype),
+    )
 
     # Batches with a common lr_eff; chunk so one owner's workspace stays bounded.
     per_slot = 2 * lay.Np * lay.Mp * 2
-    max_slots = max(1, MAX_OWNER_BYTES // per_slot)
+    step = world * max(1, MAX_OWNER_BYTES // per_slot)
     order: dict[float, list[int]] = {}
     for i, lr in enumerate(lr_effs):
         order.setdefault(float(lr), []).append(i)
-    specs = []
-    for lr_eff, idxs in order.items():
-        step = world * max_slots
-        for s in range(0, len(idxs), step):
-            specs.append(_Spec(
-                C_, ws, idxs[s : s + step], params, grads, buffers, variances, lr_eff, lay, R, C, r0, r1, g1, rank,
-                world, coeffs, fac, eps, weight_decay, cautious_wd, momentum, nesterov, maximize, muon_beta2,
-                has_var, device, momentum_done,
-            ))
+    specs = [
+        _Spec(grp, idxs[s : s + step], params, grads, buffers, variances, lr_eff)
+        for lr_eff, idxs in order.items()
+        for s in range(0, len(idxs), step)
+    ]
     _enqueue(ws, specs)
 
 
@@ -162,85 +161,106 @@ def flush(ws) -> None:
         _run_phases(pend[0], pend[1])
 
 
+@dataclass(frozen=True)
+class _Group:
+    """What every batch of one owner_compute_update call shares."""
+
+    C_: object
+    lay: object
+    R: int
+    C: int
+    rank: int
+    world: int
+    r0: int
+    r1: int
+    g1: int
+    coeffs: Tensor
+    fac: float
+    eps: float
+    weight_decay: float
+    cautious_wd: bool
+    momentum: float
+    nesterov: bool
+    maximize: bool
+    muon_beta2: float
+    has_var: bool
+    device: torch.device
+    momentum_done: bool
+    gdt: int
+    pdt: int
+
+
 class _Spec:
     """One owner-compute batch: pointer tables, symmetric-buffer layout, kernel arguments."""
 
-    def __init__(self, C_, ws, sel, params, grads, buffers, variances, lr_eff, lay, R, C, r0, r1, g1, rank, world,
-                 coeffs, fac, eps, weight_decay, cautious_wd, momentum, nesterov, maximize, muon_beta2, has_var,
-                 device, momentum_done):
-        self.C_, self.lay, self.R, self.C, self.coeffs, self.fac, self.eps = C_, lay, R, C, coeffs, fac, eps
-        self.has_var, self.device, self.muon_beta2, self.momentum_done = has_var, device, muon_beta2, momentum_done
+    def __init__(self, g: _Group, sel, params, grads, buffers, variances, lr_eff: float):
+        self.g = g
         S = len(sel)
-        self.Bo = Bo = math.ceil(S / world)
-        self.world, self.rank = world, rank
-        self.mine = max(0, min(Bo, S - rank * Bo))
-        self.slot_bytes = lay.Np * lay.Mp * 2
+        self.Bo = Bo = math.ceil(S / g.world)
+        self.mine = max(0, min(Bo, S - g.rank * Bo))
+        self.slot_bytes = g.lay.Np * g.lay.Mp * 2
+        rows = Bo * g.R * 4 if g.has_var else 0
         # Layout relative to this batch's base: sums | vbuf | rowscale | x | x2
         self.sums_rel = 0
-        self.vbuf_rel = _align(Bo * world * 4)
-        self.rs_rel = _align(self.vbuf_rel + (Bo * R * 4 if has_var else 0))
-        self.x_rel = _align(self.rs_rel + (Bo * R * 4 if has_var else 0))
+        self.vbuf_rel = _align(Bo * g.world * 4)
+        self.rs_rel = _align(self.vbuf_rel + rows)
+        self.x_rel = _align(self.rs_rel + rows)
         self.x2_rel = _align(self.x_rel + Bo * self.slot_bytes)
         self.nbytes = _align(self.x2_rel + Bo * self.slot_bytes)
-        loc = lambda t: t.to_local()  # noqa: E731
-        self.ptrs = [
-            [loc(grads[i]).data_ptr() for i in sel],
-            [loc(buffers[i]).data_ptr() for i in sel],
-            [loc(params[i]).data_ptr() for i in sel],
-            [loc(variances[i]).data_ptr() for i in sel] if has_var else [0] * S,
+        ptrs = [
+            [grads[i].to_local().data_ptr() for i in sel],
+            [buffers[i].to_local().data_ptr() for i in sel],
+            [params[i].to_local().data_ptr() for i in sel],
+            [variances[i].to_local().data_ptr() for i in sel] if g.has_var else [0] * S,
         ]
-        self.meta64 = torch.tensor(self.ptrs, dtype=torch.int64).pin_memory().to(device, non_blocking=True)
-        owner = [b // Bo for b in range(S)]
-        slot = [b % Bo for b in range(S)]
-        self.meta32 = torch.tensor([owner, slot], dtype=torch.int32).pin_memory().to(device, non_blocking=True)
-        self.gdt, self.pdt = dtype_code(grads[sel[0]].dtype), dtype_code(params[sel[0]].dtype)
-        self.geom = (r0, r1, g1)
-        self.flags = (int(nesterov), 0 if momentum_done else int(maximize), int(cautious_wd))
-        self.floats = [float(momentum), float(lr_eff), float(weight_decay)]
-        self.vec_ok = int(all(x % 16 == 0 for row in self.ptrs[:3] for x in row))
+        self.meta64 = torch.tensor(ptrs, dtype=torch.int64).pin_memory().to(g.device, non_blocking=True)
+        owner_slot = [[b // Bo for b in range(S)], [b % Bo for b in range(S)]]
+        self.meta32 = torch.tensor(owner_slot, dtype=torch.int32).pin_memory().to(g.device, non_blocking=True)
+        self.floats = [float(g.momentum), float(lr_eff), float(g.weight_decay)]
+        self.vec_ok = int(all(x % 16 == 0 for row in ptrs[:3] for x in row))
 
     def place(self, base: int) -> None:
+        g, lay = self.g, self.g.lay
         self.base = base
-        steps = self.coeffs.shape[0]
         x_off, x2_off = base + self.x_rel, base + self.x2_rel
-        res_off = x_off if steps % 2 == 0 else x2_off
-        r0, r1, g1 = self.geom
-        lay = self.lay
+        res_off = x_off if g.coeffs.shape[0] % 2 == 0 else x2_off
         self.ints = [
             x_off, res_off, base + self.sums_rel, base + self.vbuf_rel, base + self.rs_rel,
-            self.gdt, self.pdt, self.R, self.C, int(lay.transpose), lay.Np, lay.Mp, r0, r1, g1, self.rank,
-            self.world, self.flags[0], self.flags[1], self.flags[2], int(self.has_var), self.vec_ok,
+            g.gdt, g.pdt, g.R, g.C, int(lay.transpose), lay.Np, lay.Mp, g.r0, g.r1, g.g1, g.rank, g.world,
+            int(g.nesterov), 0 if g.momentum_done else int(g.maximize), int(g.cautious_wd), int(g.has_var),
+            self.vec_ok,
         ]
 
     def pack(self, peer_base):
-        self.C_.dist_pack(self.meta64, self.meta32, peer_base, self.ints, self.floats, not self.momentum_done,
-                          self.has_var)
+        g = self.g
+        g.C_.dist_pack(self.meta64, self.meta32, peer_base, self.ints, self.floats, not g.momentum_done, g.has_var)
 
     def compute(self, buf):
         if self.mine == 0:
             return
-        C_, lay, mine, base = self.C_, self.lay, self.mine, self.base
+        g, lay, mine, base = self.g, self.g.lay, self.mine, self.base
+        C_ = g.C_
 
         def region(off, n, dtype, shape):
             return buf[base + off : base + off + n].view(dtype).view(shape)
 
         x = region(self.x_rel, mine * self.slot_bytes, torch.bfloat16, (mine, lay.Np, lay.Mp))
         x2 = region(self.x2_rel, mine * self.slot_bytes, torch.bfloat16, (mine, lay.Np, lay.Mp))
-        sums = region(self.sums_rel, self.Bo * self.world * 4, torch.float32, (self.Bo, self.world))[:mine]
-        inv = C_.norm_finalize(sums.contiguous(), self.fac, self.eps)
-        a_ws = WORKSPACE.get(self.device, "a", (mine, lay.Np, lay.Np))
-        b_ws = WORKSPACE.get(self.device, "b", (mine, lay.Np, lay.Np))
-        res = C_.ortho_iterate(x, x2, a_ws, b_ws, inv, self.coeffs, 0)
-        if self.has_var:
-            R = self.R
-            rowsq = C_.row_sumsq(res, lay.transpose, R, self.C)
+        sums = region(self.sums_rel, self.Bo * g.world * 4, torch.float32, (self.Bo, g.world))[:mine]
+        inv = C_.norm_finalize(sums.contiguous(), g.fac, g.eps)
+        a_ws = WORKSPACE.get(g.device, "a", (mine, lay.Np, lay.Np))
+        b_ws = WORKSPACE.get(g.device, "b", (mine, lay.Np, lay.Np))
+        res = C_.ortho_iterate(x, x2, a_ws, b_ws, inv, g.coeffs, 0)
+        if g.has_var:
+            R = g.R
+            rowsq = C_.row_sumsq(res, lay.transpose, R, g.C)
             vbase = buf.data_ptr() + base + self.vbuf_rel
             vptrs = torch.tensor([vbase + s * R * 4 for s in range(mine)], dtype=torch.int64).pin_memory()
-            rowscale = C_.normuon_finalize(rowsq, vptrs.to(self.device, non_blocking=True), self.C, self.muon_beta2)
+            rowscale = C_.normuon_finalize(rowsq, vptrs.to(g.device, non_blocking=True), g.C, g.muon_beta2)
             region(self.rs_rel, mine * R * 4, torch.float32, (mine, R)).copy_(rowscale)
 
     def apply(self, peer_base):
-        self.C_.dist_apply(self.meta64, self.meta32, peer_base, self.ints, self.floats, self.has_var)
+        self.g.C_.dist_apply(self.meta64, self.meta32, peer_base, self.ints, self.floats, self.g.has_var)
 
 
 def _run_phases(ws, specs: list) -> None:
