@@ -2,7 +2,8 @@
 
 Same public surface as ``muonium`` (tonyf/dtensor-muon): ``Muon``, ``MuonLP``
 (+ ``Muon8bit`` / ``Muon4bit`` / ``MuonFp8``), ``MuonAlgorithm``,
-``BufferSpec``, ``OrthogonalizationStrategy`` and the algorithm registry.
+``BufferSpec``, ``OrthogonalizationStrategy`` and the algorithm registry
+(reference: ``src/muonium/__init__.py:1-28``; ``MuonLP`` needs no torchao here).
 Hot paths run hand-written sm_100a kernels from the in-tree extension
 ``dtensor_muon_b200._C``.
 """

@@ -13,6 +13,9 @@
 //   * each CTA drains its own 128 TMEM lanes; epilogue warps of both CTAs
 //     release the accumulator on the leader's barrier (remote arrive).
 // Every wait is bounded as in ortho_gemm.cu.
+// Reference counterpart: the Triton gram_nd (src/muonium/kernels/gram.py:25-106)
+// and the loops of ns_loop_triton / pe_loop_triton (newton_schulz.py:89-103,
+// polar_express.py:96-110).
 #include <ATen/cuda/CUDAContext.h>
 #include <c10/cuda/CUDAGuard.h>
 #include <torch/extension.h>

@@ -1,3 +1,6 @@
+"""Optimizers and the algorithm registry; the same exports as the reference's
+``src/muonium/optim/__init__.py:1-26``."""
+
 from .algorithms import (
     BufferSpec,
     MuonAlgorithm,

@@ -1,3 +1,6 @@
+"""Orthogonalisation entry points and loops; the same exports as the
+reference's ``src/muonium/orthogonalize/__init__.py:1-15``."""
+
 from .newton_schulz import ns_loop
 from .orthogonalize import (
     OrthogonalizationStrategy,

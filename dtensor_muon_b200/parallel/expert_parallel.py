@@ -2,6 +2,11 @@
 the matching combine, over NVLink peer memory (``backend="p2p"``) or an NCCL
 all-to-all (``backend="nccl"``, the baseline).
 
+The reference has no token exchange (it ships no model). Its EP support is the
+collective-free orthogonalisation of dim-0-sharded expert stacks
+(``src/muonium/orthogonalize/orthogonalize.py:177-204``, ``README.md:10-11``),
+which ``foreach_zeropower_3d_fsdp`` here keeps.
+
 Layout. With ``W`` ranks and ``E`` experts, rank ``r`` owns experts
 ``[r*E/W, (r+1)*E/W)``. A rank's receive region holds its tokens grouped by
 local expert, and within an expert by source rank, so the expert GEMMs consume

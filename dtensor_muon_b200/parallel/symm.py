@@ -7,6 +7,9 @@ NVSwitch. ``torch.distributed._symmetric_memory`` is used only as the
 allocator + address-exchange bootstrap; the data movement and the barrier are
 our own kernels. Barriers are bounded on the device (2 s) and report through
 the per-device error word, which :meth:`SymmetricWorkspace.check` raises on.
+
+The reference moves the same data with DTensor redistributes (NCCL all-to-alls
+in ``foreach_zeropower``, ``src/muonium/orthogonalize/orthogonalize.py:142-150``).
 """
 
 from __future__ import annotations
