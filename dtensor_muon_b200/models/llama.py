@@ -10,7 +10,6 @@ DTensor tensor-parallel plans apply without adapters.
 
 from __future__ import annotations
 
-import math
 from dataclasses import dataclass, replace
 
 import torch

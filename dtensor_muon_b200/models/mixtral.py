@@ -14,7 +14,6 @@ from __future__ import annotations
 from dataclasses import dataclass, replace
 
 import torch
-import torch.nn.functional as F
 from torch import Tensor, nn
 
 from ..ops import model_ops as _model_ops
