@@ -18,7 +18,10 @@ namespace dmb {
 namespace {
 
 constexpr int ADAM_THREADS = 256;
-constexpr int ADAM_CHUNK = 8192;  // elements per CTA
+// Elements per CTA. Large enough that the per-CTA tensor lookup (a binary search
+// over the meta table in global memory) is amortised; on the 1.05 B-param
+// embedding/head update this took the kernel from 6.98 to 6.72 ms.
+constexpr int ADAM_CHUNK = 65536;
 constexpr int META = 10;          // int64 words per tensor
 
 // meta[t] = {p, g, m, v, vmax, numel, dtypes, first_block, f32bits(step_size), f32bits(bc2_sqrt)}
