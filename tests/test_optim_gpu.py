@@ -101,6 +101,33 @@ def test_native_adam_matches_torch(amsgrad, algorithm, dtype):
         torch.testing.assert_close(x.float(), y.detach(), **tol)
 
 
+@pytest.mark.parametrize("algorithm,maximize", [("adamw", False), ("adam", True)])
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+def test_vector_adam_matches_torch(algorithm, maximize, dtype):
+    """Aligned sizes (multiples of 8) take the 16-byte vector path; the group mixes
+    tiny and large tensors so several CTAs look up their tensor in one launch."""
+    g = torch.Generator().manual_seed(3)
+    shapes = [(3 * 2048 + 16,), (64, 72), (8,), (2048,), (40, 1000)]
+    a = [nn.Parameter(torch.randn(s, generator=g).cuda().to(dtype)) for s in shapes]
+    b = [nn.Parameter(x.detach().float().clone()) for x in a]
+    opt = Muon([{"params": a, "algorithm": algorithm, "lr": 0.01, "wd": 0.1, "maximize": maximize}])
+    cls = torch.optim.AdamW if algorithm == "adamw" else torch.optim.Adam
+    ref = cls(b, lr=0.01, betas=(0.9, 0.95), weight_decay=0.1, maximize=maximize)
+    n0 = _ext.launch_count
+    for _ in range(4):
+        for x, y in zip(a, b):
+            gr = torch.randn(x.shape, generator=g).cuda()
+            x.grad = gr.to(dtype)
+            y.grad = x.grad.float().clone()
+        opt.step()
+        ref.step()
+    assert _ext.launch_count - n0 == 4, "one native AdamW launch per step"
+    tol = dict(rtol=1e-5, atol=1e-6) if dtype == torch.float32 else dict(rtol=2e-2, atol=2e-2)
+    for x, y in zip(a, b):
+        torch.testing.assert_close(x.detach().float(), y.detach(), **tol)
+    _ext.check_device_errors("cuda")
+
+
 @pytest.mark.parametrize("cls", [Muon8bit, Muon4bit, MuonFp8])
 def test_lp_fused_cuda_matches_cpu_semantics(cls):
     """Fused quantised-momentum kernels on CUDA track the CPU implementation."""
