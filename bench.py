@@ -71,20 +71,33 @@ class ClockSampler:
             self.proc.wait(timeout=5)
         except subprocess.TimeoutExpired:
             self.proc.kill()
-        rows = []
         with open(self.path) as f:
-            for line in f:
-                parts = [x.strip() for x in line.split(",")]
-                if len(parts) >= 8:
-                    rows.append(parts)
+            lines = f.readlines()
         os.unlink(self.path)
+        return self.summarize(lines)
+
+    @staticmethod
+    def summarize(lines: list[str]) -> dict:
+        """Median SM clock under load, max clock and the throttle reasons seen, from
+        ``nvidia-smi --format=csv,noheader,nounits`` lines of FIELDS. Tolerates
+        ``[N/A]`` fields and partial lines."""
+
+        def num(x):
+            try:
+                return float(x)
+            except ValueError:
+                return None
+
+        rows = [[x.strip() for x in line.split(",")] for line in lines]
+        rows = [r for r in rows if len(r) >= 8]
         if not rows:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no samples"]}
-        mhz = [float(r[1]) for r in rows if r[1].replace(".", "").isdigit()]
-        max_mhz = max(float(r[2]) for r in rows if r[2].replace(".", "").isdigit())
+        mhz = [v for v in (num(r[1]) for r in rows) if v is not None]
+        maxes = [v for v in (num(r[2]) for r in rows) if v is not None]
+        max_mhz = max(maxes) if maxes else None
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
         reasons = sorted({names[i] for r in rows for i in range(4) if r[4 + i].lower().startswith("active")})
-        loaded = [m for m in mhz if m > 0.5 * max_mhz] or mhz
+        loaded = ([m for m in mhz if m > 0.5 * max_mhz] if max_mhz else []) or mhz
         return {
             "sm_mhz": statistics.median(loaded) if loaded else None,
             "sm_max_mhz": max_mhz,
