@@ -157,9 +157,10 @@ def build_ours(args, world, device):
 
 
 def build_reference(args, world, device):
-    ref_root = os.path.join(HERE, "baseline", "_ref")
-    if not os.path.isdir(os.path.join(ref_root, "muonium")):
-        raise RuntimeError("reference not installed under baseline/_ref")
+    sys.path.insert(0, os.path.join(HERE, "baseline"))
+    from install_reference import ensure_reference
+
+    ref_root = ensure_reference()  # baseline/_ref, installed on demand from the reference source
     sys.path.insert(0, ref_root)
     # The reference pins torch 2.12.1; on this image's torch 2.11 Dynamo asserts
     # while tracing DTensor.stride() inside its compiled Muon update (FSDP runs).

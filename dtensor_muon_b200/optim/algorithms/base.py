@@ -77,26 +77,53 @@ def split_lr_scales(shape, split_sizes: tuple[int, ...]) -> tuple[float, ...]:
     return tuple(math.sqrt(max(1.0, h / cols)) / full for h in split_sizes)
 
 
-def _split_orthogonalize_full(
-    g: Tensor,
+def _orthogonalize_row_blocks(
+    mats: list[Tensor],
     split_sizes: tuple[int, ...],
-    scales: tuple[float, ...],
     *,
     ns_steps: int,
     strategy: OrthogonalizationStrategy,
-) -> Tensor:
-    """Orthogonalise row blocks of a plain 2-D tensor independently; equal-height
-    blocks share one batched call."""
-    blocks = list(g.split(list(split_sizes), dim=-2))
-    same_height: dict[int, list[int]] = {}
-    for i, blk in enumerate(blocks):
-        same_height.setdefault(blk.size(-2), []).append(i)
-    out: list[Tensor | None] = [None] * len(blocks)
-    for idxs in same_height.values():
-        us = foreach_zeropower([blocks[i] for i in idxs], steps=ns_steps, strategy=strategy)
-        for i, u in zip(idxs, us, strict=True):
-            out[i] = u * scales[i]
-    return torch.cat([u for u in out if u is not None], dim=-2)
+) -> list[Tensor]:
+    """Orthogonalise the row blocks of every (plain, same-shape) matrix of a batch.
+
+    Blocks are collected across the WHOLE batch and grouped by height, so a batch
+    of B fused QKV weights under GQA costs two engine calls (B query blocks, 2B
+    key/value blocks) rather than 2B. Each result block is scaled by its
+    :func:`split_lr_scales` factor and written in place into one preallocated
+    bf16 output per matrix (no concatenation). Same semantics as the reference's
+    per-tensor split (src/muonium/optim/algorithms/base.py:73-99).
+    """
+    if not mats:
+        return []
+    scales = split_lr_scales(mats[0].shape, split_sizes)
+    starts = [0]
+    for h in split_sizes[:-1]:
+        starts.append(starts[-1] + h)
+    outs = [torch.empty(m.shape, dtype=torch.bfloat16, device=m.device) for m in mats]
+    for height in sorted(set(split_sizes)):
+        jobs = [(k, starts[j], scales[j]) for k in range(len(mats)) for j, h in enumerate(split_sizes) if h == height]
+        us = foreach_zeropower([mats[k].narrow(-2, r0, height) for k, r0, _ in jobs], steps=ns_steps, strategy=strategy)
+        for (k, r0, sc), u in zip(jobs, us, strict=True):
+            outs[k].narrow(-2, r0, height).copy_(u * sc)
+    return outs
+
+
+def _gather_batch(gs: list[DTensor]) -> list[Tensor]:
+    """Full (replicated) local copies of a batch of DTensors with common metadata:
+    one stacked gather for the batch instead of one per tensor."""
+    try:
+        stacked = torch.stack(list(gs), dim=0)
+        return list(stacked.full_tensor().unbind(0))
+    except (RuntimeError, NotImplementedError):  # placements the stacked form cannot express
+        return [g.full_tensor() for g in gs]
+
+
+def _reshard_like(u: Tensor, like: DTensor) -> DTensor:
+    """Hand a replicated result back with ``like``'s placements; Replicate -> Shard
+    is a local slice on every rank, so no collective runs."""
+    mesh = like.device_mesh
+    rep = DTensor.from_local(u, device_mesh=mesh, placements=(Replicate(),) * mesh.ndim, run_check=False)
+    return rep.redistribute(placements=like.placements)
 
 
 def _seams_are_builtin() -> bool:
@@ -113,20 +140,12 @@ def orthogonalize_single(
     strategy: OrthogonalizationStrategy,
     split_sizes: tuple[int, ...] | None = None,
 ) -> Tensor:
-    """Orthogonalise one tensor (DTensor handling lives in ``zeropower``).
-
-    With ``split_sizes`` each row block is orthogonalised on its own and
-    rescaled (see :func:`split_lr_scales`); DTensors take a full-tensor round
-    trip so any placement works.
-    """
+    """Orthogonalise one tensor: a batch of one (DTensor handling lives in
+    ``zeropower`` and :func:`orthogonalize_batch`). With ``split_sizes`` each row
+    block is orthogonalised on its own and rescaled (:func:`split_lr_scales`)."""
     if split_sizes is None:
         return zeropower(g, steps=ns_steps, strategy=strategy)
-    scales = split_lr_scales(g.shape, split_sizes)
-    if isinstance(g, DTensor):
-        u = _split_orthogonalize_full(g.full_tensor(), split_sizes, scales, ns_steps=ns_steps, strategy=strategy)
-        u = DTensor.from_local(u, device_mesh=g.device_mesh, placements=(Replicate(),) * g.device_mesh.ndim)
-        return u.redistribute(placements=g.placements, async_op=True)
-    return _split_orthogonalize_full(g, split_sizes, scales, ns_steps=ns_steps, strategy=strategy)
+    return orthogonalize_batch([g], ns_steps=ns_steps, strategy=strategy, split_sizes=split_sizes)[0]
 
 
 def orthogonalize_batch(
@@ -138,17 +157,22 @@ def orthogonalize_batch(
 ) -> list[Tensor]:
     """Orthogonalise a same-shape batch; the only place algorithms meet distribution.
 
-    Order of preference: ``split_sizes`` handling (per tensor), the
-    collective-free path for dim-0-sharded 3-D DTensors, then the batched
-    ``foreach_zeropower``.
+    * ``split_sizes``: every row block of every matrix goes through
+      :func:`_orthogonalize_row_blocks` (one engine call per block height). A
+      DTensor batch is gathered once as a stack and its results are sliced back
+      to each rank's shard locally, so any placement works.
+    * 3-D stacks sharded only on dim 0 (FSDP / EP experts): local, collective-free.
+    * everything else: the batched ``foreach_zeropower``.
+
+    Reference behaviour: src/muonium/optim/algorithms/base.py:134-168.
     """
+    if not gs:
+        return []
     if split_sizes is not None:
         if isinstance(gs[0], DTensor):
-            return [orthogonalize_single(g, ns_steps=ns_steps, strategy=strategy, split_sizes=split_sizes) for g in gs]
-        scales = split_lr_scales(gs[0].shape, split_sizes)
-        return [
-            _split_orthogonalize_full(g, split_sizes, scales, ns_steps=ns_steps, strategy=strategy) for g in gs
-        ]
+            us = _orthogonalize_row_blocks(_gather_batch(gs), split_sizes, ns_steps=ns_steps, strategy=strategy)
+            return [_reshard_like(u, g) for u, g in zip(us, gs, strict=True)]
+        return _orthogonalize_row_blocks(list(gs), split_sizes, ns_steps=ns_steps, strategy=strategy)
     if is_fsdp_3d_sharded(gs):
         return foreach_zeropower_3d_fsdp(gs, steps=ns_steps, strategy=strategy)
     return foreach_zeropower(gs, steps=ns_steps, strategy=strategy)

@@ -38,7 +38,10 @@ def run(impl: str, steps: int = 20, load: str | None = None, save: str | None = 
               nesterov=True, use_cautious_wd=True, adam_betas=(0.9, 0.95))
     groups = [{"params": muon}, {"params": adam, "algorithm": "adamw"}]
     if impl == "reference":
-        sys.path.insert(0, os.path.join(ROOT, "baseline", "_ref"))
+        sys.path.insert(0, os.path.join(ROOT, "baseline"))
+        from install_reference import ensure_reference
+
+        sys.path.insert(0, ensure_reference())
         import muonium.optim.algorithms.base as ref_base
         from muonium import Muon as RefMuon
         from muonium.orthogonalize import foreach_zeropower, zeropower

@@ -277,3 +277,50 @@ def test_normuon_round_trip_continues_training():
         oa.step()
         oc.step()
     torch.testing.assert_close(a, c)
+
+
+def test_split_sizes_batch_groups_blocks_across_matrices(monkeypatch):
+    """Three fused weights with blocks (4, 2, 2): one engine call per block height
+    for the whole batch (3 blocks of height 4, 6 of height 2), not one per matrix."""
+    calls = []
+
+    def rec(gs, **_):
+        calls.append(len(gs))
+        return [torch.full_like(g, float(g.shape[0])).bfloat16() for g in gs]
+
+    monkeypatch.setattr(algo_base, "foreach_zeropower", rec)
+    gs = [torch.randn(8, 4) for _ in range(3)]
+    outs = algo_base.orthogonalize_batch(gs, ns_steps=5, strategy="polar_express", split_sizes=(4, 2, 2))
+    assert sorted(calls) == [3, 6]
+    scales = split_lr_scales((8, 4), (4, 2, 2))
+    for u in outs:
+        assert u.dtype == torch.bfloat16 and u.shape == (8, 4)
+        torch.testing.assert_close(u[:4].float(), torch.full((4, 4), 4.0 * scales[0]).bfloat16().float())
+        torch.testing.assert_close(u[4:].float(), torch.full((4, 4), 2.0 * scales[1]).bfloat16().float())
+
+
+def _split_dtensor_worker(rank, world):
+    import torch
+    from torch.distributed.device_mesh import init_device_mesh
+    from torch.distributed.tensor import DTensor, Shard, distribute_tensor
+
+    from dtensor_muon_b200.optim.algorithms import base
+
+    mesh = init_device_mesh("cpu", (world,))
+    torch.manual_seed(11)
+    fulls = [torch.randn(12, 8) for _ in range(3)]
+    ds = [distribute_tensor(f, mesh, [Shard(0)]) for f in fulls]
+    split = (8, 2, 2)
+    got = base.orthogonalize_batch(ds, ns_steps=5, strategy="newton_schulz", split_sizes=split)
+    want = base.orthogonalize_batch(fulls, ns_steps=5, strategy="newton_schulz", split_sizes=split)
+    for g, w in zip(got, want):
+        assert isinstance(g, DTensor) and list(g.placements) == [Shard(0)]
+        torch.testing.assert_close(g.full_tensor().float(), w.float())
+    one = base.orthogonalize_single(ds[0], ns_steps=5, strategy="newton_schulz", split_sizes=split)
+    torch.testing.assert_close(one.full_tensor().float(), want[0].float())
+
+
+def test_split_sizes_dtensor_batch_gloo():
+    from dtensor_muon_b200.testing.distributed import run_distributed
+
+    run_distributed(_split_dtensor_worker, 2)
