@@ -43,17 +43,69 @@ __device__ __forceinline__ float block_max(float v, float* red) {
   return red[0];
 }
 
-// Nearest entry of a sorted map (binary search, ties to the lower index).
-__device__ __forceinline__ int nearest_code(const float* qmap, int n, float x) {
-  int lo = 0, hi = n - 1;
-  while (hi - lo > 1) {
-    const int mid = (lo + hi) >> 1;
-    if (qmap[mid] <= x)
-      lo = mid;
-    else
-      hi = mid;
+// Nearest entry of a dynamic-tree code map, ties to the lower index, in closed
+// form (no search). The map (dynamic_tree_map in optim_lp.py) is sorted: P
+// negative magnitudes, Z zeros, P positive magnitudes (unsigned: 1 zero, then
+// P). Decade k (0 <= k < V) holds n_k = 2^(V-k-1) magnitudes
+// (0.1 + 0.9 (i+1)/n_k) 10^-k, i < n_k, so the magnitudes <= t > 0 number
+//   (2^(V-k-1) - 1) + clamp(floor((t 10^k - 0.1) n_k / 0.9), 0, n_k),
+// where k is t's decade (t in (10^-(k+1), 10^-k]); this count is exact even
+// when k is off by one at a decade edge. From it, lo = (entries <= x) - 1; one
+// comparison each way against the map absorbs float rounding at exact code
+// values, then the nearer of lo, lo + 1 is taken as the binary search would.
+struct TreeMap {
+  const float* q;   // the map, in shared memory
+  int n;            // entries (16 or 256)
+  int V;            // magnitude bits
+  int P;            // positive magnitudes (2^V - 1)
+  int neg0;         // index of the first entry >= 0 (P when signed, else 0)
+
+  // A signed map starts at -1, an unsigned one at 0.
+  __device__ TreeMap(const float* smem_map, int entries) : q(smem_map), n(entries) {
+    const int bits = entries == 256 ? 8 : 4;
+    const bool sgn = entries > 0 && smem_map[0] < 0.f;
+    V = sgn ? bits - 1 : bits;
+    P = (1 << V) - 1;
+    neg0 = sgn ? P : 0;
   }
-  return (fabsf(qmap[hi] - x) < fabsf(x - qmap[lo])) ? hi : lo;
+};
+
+__device__ __forceinline__ int tree_count_le(float t, int V) {
+  // magnitudes <= t, t >= 0
+  float pw = 1.f;   // 10^-k
+  float up = 1.f;   // 10^k
+  int k = 0;
+#pragma unroll
+  for (int j = 1; j < 8; ++j) {
+    if (j < V && t <= pw * 0.1f) {
+      pw *= 0.1f;
+      up *= 10.f;
+      k = j;
+    }
+  }
+  if (k == V - 1 && t < pw * 0.1f) return 0;  // below the smallest decade
+  const int nk = 1 << (V - k - 1);
+  const float f = floorf((t * up - 0.1f) * (float)nk / 0.9f);
+  const int in_dec = (int)fminf(fmaxf(f, 0.f), (float)nk);
+  return (nk - 1) + in_dec;
+}
+
+__device__ __forceinline__ int nearest_code(const TreeMap& m, float x) {
+  int le;  // entries <= x
+  if (x >= 0.f) {
+    le = m.neg0 + (m.n - m.neg0 - m.P) + tree_count_le(x, m.V);
+  } else {
+    // negatives <= x: magnitudes >= |x| = P - (magnitudes < |x|); magnitudes < |x|
+    // equals those <= |x| except at an exact code value, fixed below
+    le = m.P - tree_count_le(-x, m.V);
+  }
+  int lo = min(max(le - 1, 0), m.n - 2);
+  if (lo + 1 <= m.n - 2 && m.q[lo + 1] <= x) ++lo;
+  if (lo + 1 <= m.n - 2 && m.q[lo + 1] <= x) ++lo;
+  if (lo > 0 && m.q[lo] > x) --lo;
+  if (lo > 0 && m.q[lo] > x) --lo;
+  const int hi = lo + 1;
+  return (fabsf(m.q[hi] - x) < fabsf(x - m.q[lo])) ? hi : lo;
 }
 
 __device__ __forceinline__ float decode(const uint8_t* codes, int fmt, long long i, const float* qmap) {
@@ -83,13 +135,21 @@ struct LpArgs {
   const float* quant_in;  // quantise-only mode: fp32 source
 };
 
-// One CTA per quantisation block. Each thread keeps its elements in registers
-// between the absmax reduction and the requantisation.
+__device__ __forceinline__ float lp_update(const LpArgs& a, float m, float g, long long i) {
+  if (a.maximize) g = -g;
+  m = fmaf(m, a.momentum, g);
+  if (a.gout) a.gout[i] = __float2bfloat16_rn(a.nesterov ? fmaf(m, a.momentum, g) : m);
+  return m;
+}
+
+// Generic path: one CTA per quantisation block, element e of the block on
+// thread e % LP_THREADS; any block size <= 4096 and any alignment.
 __global__ void __launch_bounds__(LP_THREADS) lp_step_kernel(const LpArgs a) {
   __shared__ float qmap[256];
   __shared__ float red[LP_THREADS / 32];
   for (int i = threadIdx.x; i < a.qn; i += LP_THREADS) qmap[i] = a.qmap_g[i];
   __syncthreads();
+  const TreeMap tm(qmap, a.qn);
   const long long b0 = (long long)blockIdx.x * a.block;
   const int len = (int)min((long long)a.block, a.n - b0);
   constexpr int PER = 16;  // supports block <= LP_THREADS * PER = 4096
@@ -107,11 +167,9 @@ __global__ void __launch_bounds__(LP_THREADS) lp_step_kernel(const LpArgs a) {
       } else {
         m = decode(a.codes, a.fmt, i, qmap) * s_old;
         if (a.has_grad) {
-          float g = a.grad_dtype == 0 ? reinterpret_cast<const float*>(a.grad)[i]
-                                      : __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(a.grad)[i]);
-          if (a.maximize) g = -g;
-          m = fmaf(m, a.momentum, g);
-          if (a.gout) a.gout[i] = __float2bfloat16_rn(a.nesterov ? fmaf(m, a.momentum, g) : m);
+          const float g = a.grad_dtype == 0 ? reinterpret_cast<const float*>(a.grad)[i]
+                                            : __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(a.grad)[i]);
+          m = lp_update(a, m, g, i);
         }
       }
       if (a.dequant_out) a.dequant_out[i] = m;
@@ -125,14 +183,12 @@ __global__ void __launch_bounds__(LP_THREADS) lp_step_kernel(const LpArgs a) {
   const float inv = s_new > 0.f ? 1.f / s_new : 0.f;
   if (threadIdx.x == 0) a.scale[blockIdx.x] = s_new;
   if (a.fmt == 2) {
-    // Two codes per byte: thread handles element pairs (2t, 2t+1) of each 512-chunk.
-    __syncthreads();
-    // Stage the block through shared memory so pairs can be packed by one thread.
+    // Two codes per byte: stage the block's codes in shared memory, then pack pairs.
     __shared__ uint8_t c4[4096];
 #pragma unroll
     for (int k = 0; k < PER; ++k) {
       const int e = threadIdx.x + k * LP_THREADS;
-      if (e < len) c4[e] = (uint8_t)nearest_code(qmap, a.qn, vals[k] * inv);
+      if (e < len) c4[e] = (uint8_t)nearest_code(tm, vals[k] * inv);
     }
     __syncthreads();
     for (int e2 = threadIdx.x; e2 < (len + 1) / 2; e2 += LP_THREADS) {
@@ -152,19 +208,177 @@ __global__ void __launch_bounds__(LP_THREADS) lp_step_kernel(const LpArgs a) {
         __nv_fp8_e4m3 q(x);
         c = q.__x;
       } else {
-        c = (uint8_t)nearest_code(qmap, a.qn, x);
+        c = (uint8_t)nearest_code(tm, x);
       }
       a.codes[b0 + e] = c;
     }
   }
 }
 
-void launch_lp(const LpArgs& a) {
+// Vector path: every thread owns runs of 8 consecutive elements (16-byte bf16
+// loads/stores, 8-byte / 4-byte code accesses), so a 2048-element block is one
+// 8-element run per thread and a 4096-element block two. Requires block % 8 == 0,
+// n % 8 == 0 and 16-byte-aligned element pointers (checked on the host).
+constexpr int LP_VEC = 8;
+constexpr int LP_RUNS = 4096 / (LP_VEC * LP_THREADS);  // 2
+
+template <int FMT>
+__device__ __forceinline__ void decode8(const LpArgs& a, long long i, const float* qmap, float* v) {
+  if constexpr (FMT == 0) {
+    const uint2 w = *reinterpret_cast<const uint2*>(a.codes + i);
+    const uint32_t ws[2] = {w.x, w.y};
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      __nv_fp8_e4m3 c;
+      c.__x = (ws[j >> 2] >> (8 * (j & 3))) & 0xff;
+      v[j] = float(c);
+    }
+  } else if constexpr (FMT == 1) {
+    const uint2 w = *reinterpret_cast<const uint2*>(a.codes + i);
+    const uint32_t ws[2] = {w.x, w.y};
+#pragma unroll
+    for (int j = 0; j < 8; ++j) v[j] = qmap[(ws[j >> 2] >> (8 * (j & 3))) & 0xff];
+  } else {
+    const uint32_t w = *reinterpret_cast<const uint32_t*>(a.codes + (i >> 1));
+#pragma unroll
+    for (int j = 0; j < 8; ++j) v[j] = qmap[(w >> (4 * j)) & 15];
+  }
+}
+
+template <int FMT>
+__device__ __forceinline__ void encode8(const LpArgs& a, long long i, const TreeMap& tm, const float* v, float inv) {
+  if constexpr (FMT == 2) {
+    uint32_t w = 0;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) w |= (uint32_t)nearest_code(tm, v[j] * inv) << (4 * j);
+    *reinterpret_cast<uint32_t*>(a.codes + (i >> 1)) = w;
+  } else {
+    uint32_t ws[2] = {0u, 0u};
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      uint32_t c;
+      if constexpr (FMT == 0) {
+        __nv_fp8_e4m3 q(v[j] * inv);
+        c = q.__x;
+      } else {
+        c = (uint32_t)nearest_code(tm, v[j] * inv);
+      }
+      ws[j >> 2] |= c << (8 * (j & 3));
+    }
+    *reinterpret_cast<uint2*>(a.codes + i) = make_uint2(ws[0], ws[1]);
+  }
+}
+
+template <int FMT>
+__global__ void __launch_bounds__(LP_THREADS) lp_step_vec_kernel(const LpArgs a) {
+  __shared__ float qmap[256];
+  __shared__ float red[LP_THREADS / 32];
+  if (FMT != 0)
+    for (int i = threadIdx.x; i < a.qn; i += LP_THREADS) qmap[i] = a.qmap_g[i];
+  __syncthreads();
+  const TreeMap tm(qmap, a.qn);
+  const long long b0 = (long long)blockIdx.x * a.block;
+  const int len = (int)min((long long)a.block, a.n - b0);
+  const float s_old = a.quant_in ? 0.f : a.scale[blockIdx.x];
+  float v[LP_RUNS][LP_VEC];
+  float amax = 0.f;
+#pragma unroll
+  for (int r = 0; r < LP_RUNS; ++r) {
+    const int e = (r * LP_THREADS + threadIdx.x) * LP_VEC;
+    if (e < len) {
+      const long long i = b0 + e;
+      if (a.quant_in) {
+        const float4 x0 = *reinterpret_cast<const float4*>(a.quant_in + i);
+        const float4 x1 = *reinterpret_cast<const float4*>(a.quant_in + i + 4);
+        v[r][0] = x0.x; v[r][1] = x0.y; v[r][2] = x0.z; v[r][3] = x0.w;
+        v[r][4] = x1.x; v[r][5] = x1.y; v[r][6] = x1.z; v[r][7] = x1.w;
+      } else {
+        decode8<FMT>(a, i, qmap, v[r]);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) v[r][j] *= s_old;
+        if (a.has_grad) {
+          float g[8];
+          if (a.grad_dtype == 0) {
+            const float4 g0 = *reinterpret_cast<const float4*>(reinterpret_cast<const float*>(a.grad) + i);
+            const float4 g1 = *reinterpret_cast<const float4*>(reinterpret_cast<const float*>(a.grad) + i + 4);
+            g[0] = g0.x; g[1] = g0.y; g[2] = g0.z; g[3] = g0.w;
+            g[4] = g1.x; g[5] = g1.y; g[6] = g1.z; g[7] = g1.w;
+          } else {
+            const uint4 w = *reinterpret_cast<const uint4*>(reinterpret_cast<const __nv_bfloat16*>(a.grad) + i);
+            const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&w);
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+              const float2 f = __bfloat1622float2(h[j]);
+              g[2 * j] = f.x;
+              g[2 * j + 1] = f.y;
+            }
+          }
+          uint4 out;
+          __nv_bfloat162* o = reinterpret_cast<__nv_bfloat162*>(&out);
+#pragma unroll
+          for (int j = 0; j < 8; ++j) {
+            const float gj = a.maximize ? -g[j] : g[j];
+            v[r][j] = fmaf(v[r][j], a.momentum, gj);
+            g[j] = a.nesterov ? fmaf(v[r][j], a.momentum, gj) : v[r][j];
+          }
+#pragma unroll
+          for (int j = 0; j < 4; ++j) o[j] = __floats2bfloat162_rn(g[2 * j], g[2 * j + 1]);
+          if (a.gout) *reinterpret_cast<uint4*>(a.gout + i) = out;
+        }
+      }
+      if (a.dequant_out) {
+        *reinterpret_cast<float4*>(a.dequant_out + i) = make_float4(v[r][0], v[r][1], v[r][2], v[r][3]);
+        *reinterpret_cast<float4*>(a.dequant_out + i + 4) = make_float4(v[r][4], v[r][5], v[r][6], v[r][7]);
+      }
+    } else {
+#pragma unroll
+      for (int j = 0; j < 8; ++j) v[r][j] = 0.f;
+    }
+#pragma unroll
+    for (int j = 0; j < 8; ++j) amax = fmaxf(amax, fabsf(v[r][j]));
+  }
+  if (!a.has_grad && !a.quant_in) return;  // dequantise-only
+  amax = block_max(amax, red);
+  const float s_new = FMT == 0 ? amax / 448.f : amax;
+  const float inv = s_new > 0.f ? 1.f / s_new : 0.f;
+  if (threadIdx.x == 0) a.scale[blockIdx.x] = s_new;
+#pragma unroll
+  for (int r = 0; r < LP_RUNS; ++r) {
+    const int e = (r * LP_THREADS + threadIdx.x) * LP_VEC;
+    if (e < len) encode8<FMT>(a, b0 + e, tm, v[r], inv);
+  }
+}
+
+bool lp_vec_ok(const LpArgs& a) {
+  auto al = [](const void* p, uintptr_t m) { return (reinterpret_cast<uintptr_t>(p) & (m - 1)) == 0; };
+  if (a.block % LP_VEC != 0 || a.n % LP_VEC != 0) return false;
+  if (!al(a.codes, a.fmt == 2 ? 4 : 8)) return false;
+  if (a.grad && !al(a.grad, 16)) return false;
+  if (a.gout && !al(a.gout, 16)) return false;
+  if (a.dequant_out && !al(a.dequant_out, 16)) return false;
+  if (a.quant_in && !al(a.quant_in, 16)) return false;
+  return true;
+}
+
+void launch_lp(LpArgs a) {
   TORCH_CHECK(a.block > 0 && a.block <= 4096, "MuonLP block size must be in (0, 4096]");
   TORCH_CHECK(a.fmt != 2 || a.block % 2 == 0, "4-bit state needs an even block size");
+  if (a.fmt != 0) {
+    TORCH_CHECK(a.qn == 16 || a.qn == 256, "code map must have 16 or 256 entries");
+  }
   const long long nblocks = (a.n + a.block - 1) / a.block;
   if (nblocks == 0) return;
-  lp_step_kernel<<<(unsigned)nblocks, LP_THREADS, 0, at::cuda::getCurrentCUDAStream()>>>(a);
+  auto stream = at::cuda::getCurrentCUDAStream();
+  if (lp_vec_ok(a)) {
+    if (a.fmt == 0)
+      lp_step_vec_kernel<0><<<(unsigned)nblocks, LP_THREADS, 0, stream>>>(a);
+    else if (a.fmt == 1)
+      lp_step_vec_kernel<1><<<(unsigned)nblocks, LP_THREADS, 0, stream>>>(a);
+    else
+      lp_step_vec_kernel<2><<<(unsigned)nblocks, LP_THREADS, 0, stream>>>(a);
+  } else {
+    lp_step_kernel<<<(unsigned)nblocks, LP_THREADS, 0, stream>>>(a);
+  }
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 

@@ -18,7 +18,10 @@ algorithm's normal update and requantises.
 
 from __future__ import annotations
 
+import math
+
 import torch
+import torch.utils._pytree as pytree
 from torch import Tensor
 from torch.distributed.tensor import DTensor
 
@@ -77,10 +80,40 @@ def _nearest_codes(x: Tensor, qmap: Tensor) -> Tensor:
     return torch.where(pick_hi, hi, lo).to(torch.uint8)
 
 
-class QuantizedState:
+_aten = torch.ops.aten
+
+
+class QuantizedState(torch.Tensor):
     """Block-quantised fp32 tensor: ``codes`` (uint8), ``scale`` (fp32, one per
     block), the code map ``qmap``, ``fmt`` (0 fp8 e4m3, 1 8-bit map, 2 4-bit
-    map), ``block_size``, ``signed`` and the logical ``shape``."""
+    map), ``block_size``, ``signed`` and the logical ``shape``.
+
+    It is a ``torch.Tensor`` wrapper subclass with the logical shape and dtype
+    float32, so it can be the local tensor of a DTensor: a quantised momentum of
+    a sharded parameter keeps that parameter's mesh and placements (the
+    reference does the same with torchao subclasses,
+    src/muonium/optim/optim_lp.py:92-101). Semantics of tensor operations:
+
+    * ``detach`` / ``alias`` / same-shape ``view``: a QuantizedState sharing
+      the same codes and scales;
+    * ``copy_`` into it: requantise the source (a QuantizedState source with
+      the same format and block size is copied code for code, losslessly);
+    * ``to`` / ``cpu`` / ``cuda`` (``_to_copy``): move codes and scales; the
+      requested dtype is ignored because the state is logically fp32 (this
+      keeps it quantised through ``Optimizer.load_state_dict``'s cast);
+    * every other operation sees the dequantised fp32 values and returns
+      plain tensors (so ``narrow``, arithmetic and checkpoint readers work).
+    """
+
+    codes: Tensor
+    scale: Tensor
+    qmap: Tensor
+
+    @staticmethod
+    def __new__(cls, codes: Tensor, scale: Tensor, qmap: Tensor, fmt: int, block_size: int, signed: bool, shape):
+        return torch.Tensor._make_wrapper_subclass(
+            cls, torch.Size(shape), dtype=torch.float32, device=codes.device, requires_grad=False
+        )
 
     def __init__(self, codes: Tensor, scale: Tensor, qmap: Tensor, fmt: int, block_size: int, signed: bool, shape):
         self.codes = codes
@@ -89,14 +122,52 @@ class QuantizedState:
         self.fmt = int(fmt)
         self.block_size = int(block_size)
         self.signed = bool(signed)
-        self.shape = torch.Size(shape)
+
+    # -- subclass protocol -------------------------------------------------
+    def __tensor_flatten__(self):
+        return ["codes", "scale", "qmap"], (self.fmt, self.block_size, self.signed, tuple(self.shape))
+
+    @staticmethod
+    def __tensor_unflatten__(inner, meta, outer_size, outer_stride):
+        fmt, block_size, signed, shape = meta
+        return QuantizedState(inner["codes"], inner["scale"], inner["qmap"], fmt, block_size, signed, shape)
+
+    __torch_function__ = torch._C._disabled_torch_function_impl
+
+    def _alias(self, shape=None) -> "QuantizedState":
+        return QuantizedState(self.codes, self.scale, self.qmap, self.fmt, self.block_size, self.signed,
+                              self.shape if shape is None else shape)
+
+    def _moved(self, device) -> "QuantizedState":
+        return QuantizedState(self.codes.to(device), self.scale.to(device), self.qmap.to(device), self.fmt,
+                              self.block_size, self.signed, self.shape)
+
+    @classmethod
+    def __torch_dispatch__(cls, func, types, args=(), kwargs=None):
+        kwargs = kwargs or {}
+        if func in (_aten.detach.default, _aten.alias.default):
+            return args[0]._alias()
+        if func in (_aten.view.default, _aten._unsafe_view.default, _aten.reshape.default):
+            src, shape = args[0], args[1]
+            if isinstance(src, QuantizedState) and src.numel() == math.prod(shape) and -1 not in shape:
+                return src._alias(shape)
+        if func is _aten.copy_.default and isinstance(args[0], QuantizedState):
+            return args[0]._assign(args[1])
+        if func is _aten._to_copy.default and isinstance(args[0], QuantizedState):
+            dev = kwargs.get("device")
+            return args[0]._moved(dev if dev is not None else args[0].device)
+        if func is _aten.is_pinned.default:
+            return args[0].codes.is_pinned()
+
+        def plain(x):
+            return x.dequantize() if isinstance(x, QuantizedState) else x
+
+        return func(*pytree.tree_map(plain, args), **pytree.tree_map(plain, kwargs))
 
     # -- construction ------------------------------------------------------
     @classmethod
     def zeros(cls, shape, fmt: int, block_size: int, signed: bool, device) -> "QuantizedState":
-        n = 1
-        for s in shape:
-            n *= int(s)
+        n = math.prod(int(s) for s in shape)
         nbytes = (n + 1) // 2 if fmt == FMT_4BIT else n
         qmap = qmap_for(fmt, signed, torch.device(device))
         zero_code = 0
@@ -107,30 +178,8 @@ class QuantizedState:
         scale = torch.zeros((n + block_size - 1) // block_size, dtype=torch.float32, device=device)
         return cls(codes, scale, qmap, fmt, block_size, signed, shape)
 
-    # -- tensor-like surface -----------------------------------------------
-    @property
-    def device(self) -> torch.device:
-        return self.codes.device
-
-    @property
-    def dtype(self) -> torch.dtype:
-        return torch.float32
-
-    def numel(self) -> int:
-        n = 1
-        for s in self.shape:
-            n *= s
-        return n
-
-    def dim(self) -> int:
-        return len(self.shape)
-
-    ndim = property(dim)
-
-    def size(self, d=None):
-        return self.shape if d is None else self.shape[d]
-
     def dequantize(self) -> Tensor:
+        """The fp32 values (a plain tensor of this state's shape)."""
         n = self.numel()
         if self.codes.is_cuda:
             out = _ext.load().lp_dequantize(self.codes, self.scale, self.qmap, self.fmt, self.block_size, n)
@@ -146,9 +195,23 @@ class QuantizedState:
             vals = self.qmap[torch.stack([lo, hi], dim=1).reshape(-1)[:n]]
         return (vals * scale).view(self.shape)
 
-    def copy_(self, src: Tensor) -> "QuantizedState":
-        """Requantise from an fp32 tensor with this state's shape."""
-        x = src.detach().to(self.device, torch.float32).contiguous().view(-1)
+    def _assign(self, src) -> "QuantizedState":
+        if isinstance(src, QuantizedState) and (src.fmt, src.block_size, src.signed, src.numel()) == (
+            self.fmt, self.block_size, self.signed, self.numel()
+        ):
+            self.codes.copy_(src.codes)
+            self.scale.copy_(src.scale)
+            return self
+        if isinstance(src, QuantizedState):
+            src = src.dequantize()
+        return self._requantize(src)
+
+    def copy_(self, src, non_blocking: bool = False) -> "QuantizedState":
+        """Requantise from ``src`` (fp32 values of this state's shape)."""
+        return self._assign(src)
+
+    def _requantize(self, src: Tensor) -> "QuantizedState":
+        x = src.detach().to(self.codes.device, torch.float32).contiguous().view(-1)
         if self.codes.is_cuda:
             _ext.load().lp_quantize(x, self.codes, self.scale, self.qmap, self.fmt, self.block_size)
             return self
@@ -174,14 +237,17 @@ class QuantizedState:
             self.codes.copy_(codes)
         return self
 
-    def to(self, device) -> "QuantizedState":
-        return QuantizedState(
-            self.codes.to(device), self.scale.to(device), self.qmap.to(device), self.fmt, self.block_size,
-            self.signed, self.shape,
-        )
-
-    def __repr__(self) -> str:
+    def __repr__(self, *, tensor_contents=None) -> str:
         return f"QuantizedState(shape={tuple(self.shape)}, fmt={self.fmt}, block_size={self.block_size})"
+
+
+def local_quantized(x) -> "QuantizedState | None":
+    """The QuantizedState behind ``x`` (itself, or a DTensor's local tensor), else None."""
+    if isinstance(x, QuantizedState):
+        return x
+    if isinstance(x, DTensor) and isinstance(x._local_tensor, QuantizedState):
+        return x._local_tensor
+    return None
 
 
 try:  # allow torch.load(weights_only=True) of MuonLP checkpoints
@@ -272,7 +338,7 @@ class MuonLP(Muon):
     def muon(self, algorithm: MuonAlgorithm, params, grads, state, lr_ratios, **kw):
         if not params:
             return
-        quant_keys = [k for k, v in state.items() if any(isinstance(b, QuantizedState) for b in v)]
+        quant_keys = [k for k, v in state.items() if any(local_quantized(b) is not None for b in v)]
         if not quant_keys:
             return super().muon(algorithm, params, grads, state, lr_ratios, **kw)
         opts = {k: v for k, v in kw.items() if k not in ("foreach",)}
@@ -308,8 +374,10 @@ class MuonLP(Muon):
                 for i in sel:
                     g = grads[i]
                     for k in state:
-                        q = state[k][i]
-                        if isinstance(q, QuantizedState):
+                        q = local_quantized(state[k][i])
+                        if q is None:
+                            q = state[k][i]
+                        else:
                             t = q.dequantize()
                             if isinstance(g, DTensor):
                                 t = DTensor.from_local(
@@ -330,8 +398,8 @@ class MuonLP(Muon):
     def _fused_lp(self, algorithm, p, g, st, lr_ratio, opts):
         """Step the quantised momentum of one tensor; returns (param, g', variance, lr_eff)
         for the batched orthogonalisation, or None when the fused path does not apply."""
-        q = st.get("momentum_buffer")
-        if not isinstance(q, QuantizedState) or not q.codes.is_cuda:
+        q = local_quantized(st.get("momentum_buffer"))
+        if q is None or not q.codes.is_cuda:
             return None
         if type(algorithm) not in (MuonBaseline, NorMuon) or not algo_base._seams_are_builtin():
             return None
@@ -351,7 +419,7 @@ class MuonLP(Muon):
         variances = None
         if isinstance(algorithm, NorMuon):
             v = to_local(st["variance_neuron"])
-            if isinstance(v, QuantizedState) or not (v.is_cuda and v.is_contiguous()):
+            if local_quantized(v) is not None or not (v.is_cuda and v.is_contiguous()):
                 return None
             variances = [v]
         g_eff = torch.empty(g.shape, dtype=torch.bfloat16, device=g.device)

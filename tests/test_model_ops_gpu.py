@@ -54,3 +54,23 @@ def test_cross_entropy_fwd_bwd(T, V):
     loss.backward()
     ref.backward()
     torch.testing.assert_close(logits.grad.float(), ref_in.grad, rtol=2e-2, atol=1e-4)
+
+
+def test_swiglu_and_rope_through_the_test_kit():
+    """Fused kernels vs fp32 PyTorch via check_impls (forward, shared-cotangent
+    backward, CUDA-event timing with L2 flush)."""
+    from testkit import check_impls
+
+    torch.manual_seed(2)
+    a = torch.randn(1024, 2048, device="cuda").bfloat16().requires_grad_()
+    b = torch.randn(1024, 2048, device="cuda").bfloat16().requires_grad_()
+    times = check_impls(
+        {"dmb.swiglu": model_ops.swiglu},
+        {"torch_fp32": lambda x, y: (F.silu(x.float()) * y.float()), "torch_bf16": lambda x, y: F.silu(x) * y},
+        (a, b), rtol=2e-2, atol=2e-2, bwd=True,
+    )
+    assert set(times) == {"dmb.swiglu", "torch_fp32", "torch_bf16"} and all(t > 0 for t in times.values())
+    cos, sin = rope_tables(128, 512, 10000.0, "cuda")
+    x = torch.randn(2, 512, 8, 128, device="cuda").bfloat16().requires_grad_()
+    check_impls(lambda t: model_ops.rope(t, cos, sin), lambda t: model_ops.rope_reference(t.float(), cos, sin),
+                (x,), rtol=2e-2, atol=3e-2, bwd=True, bench=False)

@@ -34,12 +34,24 @@ def _run(opt, params, steps=3, seed=123, dtype=torch.float32):
 @pytest.mark.parametrize("cautious", [True, False])
 @pytest.mark.parametrize("nesterov", [True, False])
 @pytest.mark.parametrize("wd", [0.0, 0.3])
-def test_foreach_matches_per_param(strategy, cautious, nesterov, wd):
+def test_foreach_matches_per_param(monkeypatch, strategy, cautious, nesterov, wd):
+    """Fused foreach kernels vs the per-parameter PyTorch formulation with the
+    PyTorch orthogonalisation loop (no native kernel on that side)."""
+    from dtensor_muon_b200.orthogonalize import orthogonalize as om
+
     kw = dict(lr=0.2, wd=wd, nesterov=nesterov, use_cautious_wd=cautious, orthogonalization_strategy=strategy)
     a, b = _params(0), _params(0)
-    oa, ob = Muon(a, foreach=False, **kw), Muon(b, foreach=True, **kw)
+    monkeypatch.setattr(algo_base, "zeropower", lambda g, **k: om.zeropower(g, use_native=False, **k))
+    monkeypatch.setattr(algo_base, "foreach_zeropower",
+                        lambda gs, **k: om.foreach_zeropower(gs, use_native=False, **k))
+    oa = Muon(a, foreach=False, **kw)
+    n0 = _ext.launch_count
     _run(oa, a)
+    assert _ext.launch_count == n0, "the per-parameter torch side must not launch native kernels"
+    monkeypatch.undo()
+    ob = Muon(b, foreach=True, **kw)
     _run(ob, b)
+    assert _ext.launch_count > n0
     for x, y in zip(a, b):
         assert_close(y, x, rtol=RTOL, atol=ATOL, max_mismatch_pct=PCT)
     _ext.check_device_errors("cuda")
@@ -160,6 +172,33 @@ def test_lp_quantize_kernel_matches_cpu():
         same = (qg.codes.cpu() == qc.codes).float().mean().item()
         assert same > 0.999, (fmt, same)
         torch.testing.assert_close(qg.dequantize().cpu(), qc.dequantize(), rtol=0, atol=1e-6)
+
+
+@pytest.mark.parametrize("n,block", [(8192, 2048), (16384, 4096), (4 * 1030, 1030), (8190, 1024)])
+def test_lp_kernels_vector_and_generic_paths_match_cpu(n, block):
+    """Vector path (block and n multiples of 8) and generic path (any block size)
+    of the quantise / momentum-step kernels against the CPU formulation: the
+    dynamic-tree codes (closed-form index on the GPU, search on the CPU) agree exactly."""
+    from dtensor_muon_b200.optim.optim_lp import FMT_4BIT, FMT_8BIT, FMT_FP8, QuantizedState
+
+    torch.manual_seed(1)
+    x = torch.randn(n)
+    g = torch.randn(n)
+    for fmt in (FMT_FP8, FMT_8BIT, FMT_4BIT):
+        qc = QuantizedState.zeros(x.shape, fmt, block, True, "cpu").copy_(x)
+        qg = QuantizedState.zeros(x.shape, fmt, block, True, "cuda").copy_(x.cuda())
+        torch.testing.assert_close(qg.scale.cpu(), qc.scale)
+        if fmt != FMT_FP8:
+            assert torch.equal(qg.codes.cpu(), qc.codes), fmt
+        gout = torch.empty(n, dtype=torch.bfloat16, device="cuda")
+        _ext.load().lp_momentum_step(qg.codes, qg.scale, qg.qmap, qg.fmt, block, g.cuda(), gout, 0.9, True, False)
+        m = qc.dequantize() * 0.9 + g
+        torch.testing.assert_close(gout.float().cpu(), (m * 0.9 + g).bfloat16().float(), rtol=1e-2, atol=1e-6)
+        qc.copy_(m)
+        torch.testing.assert_close(qg.scale.cpu(), qc.scale)
+        if fmt != FMT_FP8:
+            agree = (qg.codes.cpu() == qc.codes).float().mean().item()
+            assert agree > 0.999, (fmt, agree)
 
 
 def test_cpu_offload_round_trip_matches_cuda():

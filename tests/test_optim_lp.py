@@ -96,3 +96,114 @@ def test_lp_state_dict_round_trip(tmp_path):
     opt.step()
     opt2.step()
     torch.testing.assert_close(a, b)
+
+
+def _closed_form_codes(x, qmap):
+    """float32 restatement of the CUDA kernel's closed-form nearest code
+    (``nearest_code`` in ops/csrc/lp_quant.cu), vectorised with numpy."""
+    import numpy as np
+
+    q = qmap.numpy().astype(np.float32)
+    n = q.size
+    bits = 8 if n == 256 else 4
+    sgn = q[0] < 0
+    V = bits - 1 if sgn else bits
+    P = (1 << V) - 1
+    neg0 = P if sgn else 0
+    x = x.numpy().astype(np.float32)
+
+    def count_le(t):
+        pw = np.ones_like(t)
+        up = np.ones_like(t)
+        k = np.zeros(t.shape, dtype=np.int64)
+        for j in range(1, 8):
+            if j < V:
+                m = t <= pw * np.float32(0.1)
+                pw = np.where(m, pw * np.float32(0.1), pw).astype(np.float32)
+                up = np.where(m, up * np.float32(10.0), up).astype(np.float32)
+                k = np.where(m, j, k)
+        nk = (1 << (V - k - 1)).astype(np.float32)
+        f = np.floor(((t * up - np.float32(0.1)) * nk / np.float32(0.9)).astype(np.float32))
+        c = (nk - 1 + np.clip(f, 0, nk)).astype(np.int64)
+        return np.where((k == V - 1) & (t < pw * np.float32(0.1)), 0, c)
+
+    le = np.where(x >= 0, neg0 + (n - neg0 - P) + count_le(np.abs(x)), P - count_le(np.abs(x)))
+    lo = np.clip(le - 1, 0, n - 2)
+    for _ in range(2):
+        lo = np.where((lo + 1 <= n - 2) & (q[np.minimum(lo + 1, n - 1)] <= x), lo + 1, lo)
+    for _ in range(2):
+        lo = np.where((lo > 0) & (q[lo] > x), lo - 1, lo)
+    hi = lo + 1
+    return torch.from_numpy(np.where(np.abs(q[hi] - x) < np.abs(x - q[lo]), hi, lo).astype(np.uint8))
+
+
+@pytest.mark.parametrize("bits,signed", [(8, True), (4, True), (8, False), (4, False)])
+def test_closed_form_code_index_matches_search(bits, signed):
+    """The kernel's arithmetic code index equals the sorted-map search on every
+    code value, every midpoint between codes, their float neighbours and random
+    values in [-1, 1]."""
+    from dtensor_muon_b200.optim.optim_lp import _nearest_codes
+
+    qmap = dynamic_tree_map(bits, signed)
+    mids = (qmap[1:] + qmap[:-1]) / 2
+    base = torch.cat([qmap, mids, torch.rand(200000) * 2 - 1 if signed else torch.rand(200000)])
+    xs = torch.cat([base, torch.nextafter(base, torch.tensor(2.0)), torch.nextafter(base, torch.tensor(-2.0))])
+    if not signed:
+        xs = xs.clamp(min=0.0)
+    want = _nearest_codes(xs, qmap)
+    got = _closed_form_codes(xs, qmap)
+    bad = (want != got).nonzero().flatten()
+    assert bad.numel() == 0, [(xs[i].item(), want[i].item(), got[i].item()) for i in bad[:5]]
+
+
+def _lp_dcp_worker(rank, world, ckpt_dir, cls_name):
+    import torch
+    import torch.distributed.checkpoint as dcp
+    from torch.distributed.device_mesh import init_device_mesh
+    from torch.distributed.tensor import DTensor, Shard, distribute_tensor
+
+    import dtensor_muon_b200 as dmb
+    from dtensor_muon_b200.optim.optim_lp import QuantizedState
+
+    cls = getattr(dmb, cls_name)
+    mesh = init_device_mesh("cpu", (world,))
+    torch.manual_seed(0)
+    full = torch.randn(128, 64)
+    grads = [torch.randn(128, 64) for _ in range(3)]
+
+    def make():
+        p = torch.nn.Parameter(distribute_tensor(full.clone(), mesh, [Shard(0)]))
+        return p, cls([p], lr=0.02, block_size=1024)
+
+    p, opt = make()
+    for g in grads[:2]:
+        p.grad = distribute_tensor(g, mesh, [Shard(0)])
+        opt.step()
+    m = opt.state[p]["momentum_buffer"]
+    # the quantised momentum keeps the parameter's mesh and placements
+    assert isinstance(m, DTensor) and list(m.placements) == [Shard(0)] and m.shape == p.shape
+    assert isinstance(m.to_local(), QuantizedState)
+    dcp.save({"optim": opt.state_dict()}, checkpoint_id=ckpt_dir)
+
+    p2, opt2 = make()
+    p2.grad = distribute_tensor(torch.zeros(128, 64), mesh, [Shard(0)])
+    opt2.step()  # materialise state with the same structure, then load into it in place
+    with torch.no_grad():
+        p2.copy_(p)
+    sd = {"optim": opt2.state_dict()}
+    dcp.load(sd, checkpoint_id=ckpt_dir)
+    opt2.load_state_dict(sd["optim"])
+    m2 = opt2.state[p2]["momentum_buffer"]
+    assert isinstance(m2, DTensor) and isinstance(m2.to_local(), QuantizedState)
+    torch.testing.assert_close(m2.to_local().dequantize(), m.to_local().dequantize())
+    for o, q in ((opt, p), (opt2, p2)):
+        q.grad = distribute_tensor(grads[2], mesh, [Shard(0)])
+        o.step()
+    torch.testing.assert_close(p2.full_tensor(), p.full_tensor())
+
+
+@pytest.mark.parametrize("cls_name", ["Muon8bit", "Muon4bit", "MuonFp8"])
+def test_quantized_dtensor_state_dcp_round_trip_gloo(tmp_path, cls_name):
+    from dtensor_muon_b200.testing.distributed import run_distributed
+
+    run_distributed(_lp_dcp_worker, 2, args=(str(tmp_path / "ckpt"), cls_name))

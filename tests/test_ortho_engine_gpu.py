@@ -162,3 +162,21 @@ def test_engine_contracts_raise():
         C.gram_sym2(xb, out, None, None, 1.0, 0.0, 0, 0)
     with pytest.raises(AssertionError, match="only supports up to 5"):
         ortho.orthogonalize_native([torch.randn(8, 8, device="cuda")], 6, "polar_express")
+
+
+@pytest.mark.parametrize("strategy", ["newton_schulz", "polar_express"])
+def test_orthogonalize_llama_size_batch_matches_fp64(strategy):
+    """A Llama-3-8B gate/up batch (2 x 4096 x 14336, the transposed long-K path
+    of the 2-SM engine) against the fp64 PyTorch loop."""
+    torch.manual_seed(7)
+    g = torch.randn(2, 4096, 14336, device="cuda")
+    got = torch.stack(ortho.orthogonalize_native(list(g.unbind(0)), 5, strategy, 1e-7))
+    loop = ns_loop if strategy == "newton_schulz" else pe_loop
+    ref = loop(g.double(), 5, eps=1e-7).float()
+    del g
+    frac = _close_frac(got, ref, rtol=1e-2, atol=5e-2)
+    assert frac < 0.02, frac
+    # orthogonality: the singular values of the bf16 result sit near 1 (NS-5 and PE-5 leave a spread)
+    sv = torch.linalg.svdvals(got[0].float())
+    assert 0.3 < float(sv.min()) and float(sv.max()) < 1.3
+    _ext.check_device_errors("cuda")
