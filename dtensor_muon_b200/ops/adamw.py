@@ -77,7 +77,7 @@ def fused_adam(
                 dts,
                 0,
                 _f32_bits(lr / bc1),
-                _f32_bits(math.sqrt(bc2)),
+                _f32_bits(1.0 / math.sqrt(bc2)),
             ]
         )
     meta = torch.tensor(rows, dtype=torch.int64)

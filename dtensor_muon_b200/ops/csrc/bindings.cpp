@@ -61,6 +61,8 @@ void dist_apply(const at::Tensor& meta_i64, const at::Tensor& meta_i32, const at
 void dist_barrier(const at::Tensor& flag_base, int64_t rank, int64_t world, int64_t epoch);
 void push_slots(const at::Tensor& src, const at::Tensor& peer_base, int64_t off, int64_t slot_bytes, int64_t rank,
                 int64_t world, bool per_peer, int64_t max_ctas);
+void pull_slots(at::Tensor& out, const at::Tensor& peer_base, int64_t off, int64_t slot_bytes, int64_t rank,
+                int64_t world, int64_t max_ctas);
 void local_slot_sum(at::Tensor& out, const at::Tensor& staging_bytes, int64_t off, int64_t world, double scale,
                     int64_t max_ctas);
 void rs_sum_momentum(at::Tensor& out, const at::Tensor& staging_bytes, int64_t off, int64_t world, double scale,
@@ -134,6 +136,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("dist_barrier", &dmb::dist_barrier);
   m.def("push_slots", &dmb::push_slots);
   m.def("local_slot_sum", &dmb::local_slot_sum);
+  m.def("pull_slots", &dmb::pull_slots);
   m.def("rs_sum_momentum", &dmb::rs_sum_momentum);
   m.def("ep_scatter_rows", &dmb::ep_scatter_rows);
   m.def("ep_gather_rows", &dmb::ep_gather_rows);

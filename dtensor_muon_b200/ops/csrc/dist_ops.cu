@@ -57,7 +57,10 @@ struct DistArgs {
   int grad_dtype, param_dtype;
   int R, C, transpose, Np, Mp;
   int r0, r1;           // this rank's global rows [r0, r1)
-  int g1;               // rows handled by pack: [r0, g1) (last rank covers padding)
+  int g1;               // rows handled by pack: [r0, g1) (the rank ending at R also covers the padding)
+  int c0, c1;           // this rank's global columns [c0, c1) (FSDP: the whole width)
+  int h1;               // columns handled by pack: [c0, h1) (the rank ending at C covers the padding)
+  int ldl;              // row stride of the local shard (c1 - c0 for a contiguous shard)
   int rank, world;
   float momentum;
   int nesterov, maximize;
@@ -90,7 +93,7 @@ __global__ void __launch_bounds__(NT) dist_pack_rows_kernel(const DistArgs a) {
   __shared__ float red[NT / 32];
   const int b = blockIdx.y;
   const int tr = blockIdx.x / a.tiles_c, tc = blockIdx.x % a.tiles_c;
-  const int g0 = a.r0 + tr * T, c0 = tc * T;
+  const int g0 = a.r0 + tr * T, c0 = a.c0 + tc * T;
   const void* g = reinterpret_cast<const void*>(a.grad[b]);
   float* buf = a.buf ? reinterpret_cast<float*>(a.buf[b]) : nullptr;
   const int j = threadIdx.x & (T - 1), i0 = threadIdx.x >> 6;
@@ -98,8 +101,8 @@ __global__ void __launch_bounds__(NT) dist_pack_rows_kernel(const DistArgs a) {
   for (int i = i0; i < T; i += NT / T) {
     const int gr = g0 + i, c = c0 + j;
     float v = 0.f;
-    if (gr < a.r1 && c < a.C) {
-      const long long idx = (long long)(gr - a.r0) * a.C + c;
+    if (gr < a.r1 && c < a.c1) {
+      const long long idx = (long long)(gr - a.r0) * a.ldl + (c - a.c0);
       float gv = ldf(g, a.grad_dtype, idx);
       if (a.maximize) gv = -gv;
       if (buf) {
@@ -117,18 +120,17 @@ __global__ void __launch_bounds__(NT) dist_pack_rows_kernel(const DistArgs a) {
   __syncthreads();
   __nv_bfloat16* X = reinterpret_cast<__nv_bfloat16*>(a.peer_base[a.owner[b]] + a.x_off) +
                      (long long)a.slot[b] * a.Np * a.Mp;
-  const int Cpad = a.transpose ? a.Np : a.Mp;
   if (!a.transpose) {
     // X[gr][c]: row-contiguous stores.
     for (int i = i0; i < T; i += NT / T) {
       const int gr = g0 + i, c = c0 + j;
-      if (gr < a.g1 && c < Cpad) X[(long long)gr * a.Mp + c] = __float2bfloat16_rn(tile[i][j]);
+      if (gr < a.g1 && c < a.h1) X[(long long)gr * a.Mp + c] = __float2bfloat16_rn(tile[i][j]);
     }
   } else {
     // X[c][gr]: consecutive threads walk gr.
     for (int i = i0; i < T; i += NT / T) {
       const int c = c0 + i, gr = g0 + j;
-      if (gr < a.g1 && c < Cpad) X[(long long)c * a.Mp + gr] = __float2bfloat16_rn(tile[j][i]);
+      if (gr < a.g1 && c < a.h1) X[(long long)c * a.Mp + gr] = __float2bfloat16_rn(tile[j][i]);
     }
   }
   const float tot = block_sum(ss, red);
@@ -143,7 +145,7 @@ __global__ void __launch_bounds__(NT) dist_push_sums_kernel(const DistArgs a, in
   const float tot = block_sum(s, red);
   const int64_t base = a.peer_base[a.owner[b]];
   if (threadIdx.x == 0) reinterpret_cast<float*>(base + a.sums_off)[(long long)a.slot[b] * a.world + a.rank] = tot;
-  if (a.var) {
+  if (a.var && a.c0 == 0) {  // one writer per row (the rank holding the first column block)
     const float* v = reinterpret_cast<const float*>(a.var[b]);
     float* dst = reinterpret_cast<float*>(base + a.vbuf_off) + (long long)a.slot[b] * a.R;
     for (int r = a.r0 + threadIdx.x; r < a.r1; r += NT) dst[r] = v[r - a.r0];
@@ -154,7 +156,7 @@ __global__ void __launch_bounds__(NT) dist_apply_rows_kernel(const DistArgs a) {
   __shared__ float tile[T][T + 1];
   const int b = blockIdx.y;
   const int tr = blockIdx.x / a.tiles_c, tc = blockIdx.x % a.tiles_c;
-  const int g0 = a.r0 + tr * T, c0 = tc * T;
+  const int g0 = a.r0 + tr * T, c0 = a.c0 + tc * T;
   const int64_t base = a.peer_base[a.owner[b]];
   const __nv_bfloat16* U = reinterpret_cast<const __nv_bfloat16*>(base + a.res_off) + (long long)a.slot[b] * a.Np * a.Mp;
   const float* rs = a.has_rowscale ? reinterpret_cast<const float*>(base + a.rs_off) + (long long)a.slot[b] * a.R : nullptr;
@@ -162,22 +164,22 @@ __global__ void __launch_bounds__(NT) dist_apply_rows_kernel(const DistArgs a) {
   if (!a.transpose) {
     for (int i = i0; i < T; i += NT / T) {
       const int gr = g0 + i, c = c0 + j;
-      tile[i][j] = (gr < a.r1 && c < a.C) ? __bfloat162float(U[(long long)gr * a.Mp + c]) : 0.f;
+      tile[i][j] = (gr < a.r1 && c < a.c1) ? __bfloat162float(U[(long long)gr * a.Mp + c]) : 0.f;
     }
   } else {
     for (int i = i0; i < T; i += NT / T) {
       const int c = c0 + i, gr = g0 + j;
-      tile[j][i] = (gr < a.r1 && c < a.C) ? __bfloat162float(U[(long long)c * a.Mp + gr]) : 0.f;
+      tile[j][i] = (gr < a.r1 && c < a.c1) ? __bfloat162float(U[(long long)c * a.Mp + gr]) : 0.f;
     }
   }
   __syncthreads();
   void* P = reinterpret_cast<void*>(a.param[b]);
   for (int i = i0; i < T; i += NT / T) {
     const int gr = g0 + i, c = c0 + j;
-    if (gr >= a.r1 || c >= a.C) continue;
+    if (gr >= a.r1 || c >= a.c1) continue;
     float u = tile[i][j];
     if (rs) u *= rs[gr];
-    const long long idx = (long long)(gr - a.r0) * a.C + c;
+    const long long idx = (long long)(gr - a.r0) * a.ldl + (c - a.c0);
     const float pv = ldf(P, a.param_dtype, idx);
     if (a.wd != 0.f) {
       if (a.cautious) {
@@ -226,17 +228,17 @@ __global__ void __launch_bounds__(NT) dist_pack_rows_vec(const DistArgs a) {
   __shared__ float red[NT / 32];
   const int b = blockIdx.y;
   const int tr = blockIdx.x / a.tiles_c, tc = blockIdx.x % a.tiles_c;
-  const int gr = a.r0 + tr * 16 + (threadIdx.x >> 4), c = tc * 128 + (threadIdx.x & 15) * 8;
+  const int gr = a.r0 + tr * 16 + (threadIdx.x >> 4), c = a.c0 + tc * 128 + (threadIdx.x & 15) * 8;
   float v[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
   float ss = 0.f;
-  if (gr < a.r1 && c < a.C) {
-    const long long idx = (long long)(gr - a.r0) * a.C + c;
+  if (gr < a.r1 && c < a.c1) {
+    const long long idx = (long long)(gr - a.r0) * a.ldl + (c - a.c0);
     dist_momentum8(a, reinterpret_cast<const void*>(a.grad[b]), a.buf ? reinterpret_cast<float*>(a.buf[b]) : nullptr,
                    idx, v);
 #pragma unroll
     for (int k = 0; k < 8; ++k) ss = fmaf(v[k], v[k], ss);
   }
-  if (gr < a.g1 && c < a.Mp) {
+  if (gr < a.g1 && c < a.h1) {
     __nv_bfloat16* X = reinterpret_cast<__nv_bfloat16*>(a.peer_base[a.owner[b]] + a.x_off) +
                        (long long)a.slot[b] * a.Np * a.Mp;
     store8(X, 1, (long long)gr * a.Mp + c, v);
@@ -251,7 +253,7 @@ __global__ void __launch_bounds__(NT) dist_pack_tr_vec(const DistArgs a) {
   __shared__ float red[NT / 32];
   const int b = blockIdx.y;
   const int tr = blockIdx.x / a.tiles_c, tc = blockIdx.x % a.tiles_c;
-  const int g0 = a.r0 + tr * T, c0 = tc * T;
+  const int g0 = a.r0 + tr * T, c0 = a.c0 + tc * T;
   const int lane8 = (threadIdx.x & 7) * 8, row = threadIdx.x >> 3;
   const void* g = reinterpret_cast<const void*>(a.grad[b]);
   float* buf = a.buf ? reinterpret_cast<float*>(a.buf[b]) : nullptr;
@@ -261,8 +263,8 @@ __global__ void __launch_bounds__(NT) dist_pack_tr_vec(const DistArgs a) {
     const int i = row + it * 32;
     const int gr = g0 + i, c = c0 + lane8;
     float v[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-    if (gr < a.r1 && c < a.C) {
-      dist_momentum8(a, g, buf, (long long)(gr - a.r0) * a.C + c, v);
+    if (gr < a.r1 && c < a.c1) {
+      dist_momentum8(a, g, buf, (long long)(gr - a.r0) * a.ldl + (c - a.c0), v);
 #pragma unroll
       for (int k = 0; k < 8; ++k) ss = fmaf(v[k], v[k], ss);
     }
@@ -276,7 +278,7 @@ __global__ void __launch_bounds__(NT) dist_pack_tr_vec(const DistArgs a) {
   for (int it = 0; it < 2; ++it) {
     const int j = row + it * 32;  // column offset within the tile
     const int c = c0 + j, gr = g0 + lane8;
-    if (c < a.Np && gr < a.g1) {
+    if (c < a.h1 && gr < a.g1) {
       float v[8];
 #pragma unroll
       for (int k = 0; k < 8; ++k) v[k] = tile[lane8 + k][j];
@@ -294,7 +296,7 @@ __device__ __forceinline__ void dist_apply8(const DistArgs& a, int b, int gr, in
     for (int k = 0; k < 8; ++k) u[k] *= f;
   }
   void* P = reinterpret_cast<void*>(a.param[b]);
-  const long long idx = (long long)(gr - a.r0) * a.C + c;
+  const long long idx = (long long)(gr - a.r0) * a.ldl + (c - a.c0);
   float p[8];
   load8(P, a.param_dtype, idx, p);
 #pragma unroll
@@ -309,13 +311,13 @@ __device__ __forceinline__ void dist_apply8(const DistArgs& a, int b, int gr, in
 __global__ void __launch_bounds__(NT) dist_apply_rows_vec(const DistArgs a) {
   const int b = blockIdx.y;
   const int tr = blockIdx.x / a.tiles_c, tc = blockIdx.x % a.tiles_c;
-  const int gr = a.r0 + tr * 16 + (threadIdx.x >> 4), c = tc * 128 + (threadIdx.x & 15) * 8;
+  const int gr = a.r0 + tr * 16 + (threadIdx.x >> 4), c = a.c0 + tc * 128 + (threadIdx.x & 15) * 8;
   const int64_t base = a.peer_base[a.owner[b]];
   if (a.var && tc == 0 && (threadIdx.x & 15) == 0 && gr < a.r1) {
     const float* vsrc = reinterpret_cast<const float*>(base + a.vbuf_off) + (long long)a.slot[b] * a.R;
     reinterpret_cast<float*>(a.var[b])[gr - a.r0] = vsrc[gr];
   }
-  if (gr >= a.r1 || c >= a.C) return;
+  if (gr >= a.r1 || c >= a.c1) return;
   const __nv_bfloat16* U = reinterpret_cast<const __nv_bfloat16*>(base + a.res_off) + (long long)a.slot[b] * a.Np * a.Mp;
   const float* rs = a.has_rowscale ? reinterpret_cast<const float*>(base + a.rs_off) + (long long)a.slot[b] * a.R : nullptr;
   float u[8];
@@ -327,7 +329,7 @@ __global__ void __launch_bounds__(NT) dist_apply_tr_vec(const DistArgs a) {
   __shared__ float tile[T][T + 1];
   const int b = blockIdx.y;
   const int tr = blockIdx.x / a.tiles_c, tc = blockIdx.x % a.tiles_c;
-  const int g0 = a.r0 + tr * T, c0 = tc * T;
+  const int g0 = a.r0 + tr * T, c0 = a.c0 + tc * T;
   const int64_t base = a.peer_base[a.owner[b]];
   const __nv_bfloat16* U = reinterpret_cast<const __nv_bfloat16*>(base + a.res_off) + (long long)a.slot[b] * a.Np * a.Mp;
   const float* rs = a.has_rowscale ? reinterpret_cast<const float*>(base + a.rs_off) + (long long)a.slot[b] * a.R : nullptr;
@@ -336,7 +338,7 @@ __global__ void __launch_bounds__(NT) dist_apply_tr_vec(const DistArgs a) {
   for (int it = 0; it < 2; ++it) {
     const int j = row + it * 32;  // workspace row = param column c0 + j
     float v[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-    if (c0 + j < a.C && g0 + lane8 < a.r1) load8(U, 1, (long long)(c0 + j) * a.Mp + g0 + lane8, v);
+    if (c0 + j < a.c1 && g0 + lane8 < a.r1) load8(U, 1, (long long)(c0 + j) * a.Mp + g0 + lane8, v);
 #pragma unroll
     for (int k = 0; k < 8; ++k) tile[j][lane8 + k] = v[k];
   }
@@ -345,7 +347,7 @@ __global__ void __launch_bounds__(NT) dist_apply_tr_vec(const DistArgs a) {
   for (int it = 0; it < 2; ++it) {
     const int i = row + it * 32;
     const int gr = g0 + i, c = c0 + lane8;
-    if (gr >= a.r1 || c >= a.C) continue;
+    if (gr >= a.r1 || c >= a.c1) continue;
     float u[8];
 #pragma unroll
     for (int k = 0; k < 8; ++k) u[k] = tile[lane8 + k][i];
@@ -427,12 +429,24 @@ DistArgs make_args(const at::Tensor& meta_i64, const at::Tensor& meta_i32, const
   a.cautious = ints[19];
   a.has_rowscale = ints[20];
   a.vec_ok = ints.size() > 21 ? (int)ints[21] : 0;
+  // ints[22..25]: c0 c1 h1 ldl (column block of a 2-D sharded shard); default: all columns
+  const int Cpad = a.transpose ? a.Np : a.Mp;
+  a.c0 = ints.size() > 25 ? (int)ints[22] : 0;
+  a.c1 = ints.size() > 25 ? (int)ints[23] : a.C;
+  a.h1 = ints.size() > 25 ? (int)ints[24] : Cpad;
+  a.ldl = ints.size() > 25 ? (int)ints[25] : a.C;
   a.momentum = floats[0];
   a.lr_eff = floats[1];
   a.wd = floats[2];
   return a;
 }
 }  // namespace
+
+// 8-element vector kernels: every row/column edge they touch is a multiple of 8.
+bool vec_shape_ok(const DistArgs& a) {
+  return a.vec_ok && a.C % 8 == 0 && a.R % 8 == 0 && a.r0 % 8 == 0 && a.r1 % 8 == 0 && a.c0 % 8 == 0 &&
+         a.c1 % 8 == 0 && a.h1 % 8 == 0 && a.ldl % 8 == 0;
+}
 
 // Phase 1: local momentum + P2P scatter into owners' workspaces, then per-matrix
 // sums (and NorMuon variance rows) pushed to the owners.
@@ -441,17 +455,17 @@ void dist_pack(const at::Tensor& meta_i64, const at::Tensor& meta_i32, const at:
   const at::cuda::CUDAGuard guard(meta_i64.device());
   DistArgs a = make_args(meta_i64, meta_i32, peer_base, ints, floats, has_buf, has_var);
   const int B = meta_i64.size(1);
-  const int Cpad = a.transpose ? a.Np : a.Mp;
-  a.tiles_c = (Cpad + T - 1) / T;
+  const int width = a.h1 - a.c0;
+  a.tiles_c = (width + T - 1) / T;
   const int rows = a.g1 - a.r0;
   const int tiles_r = rows > 0 ? (rows + T - 1) / T : 0;
-  const int nblk = tiles_r * a.tiles_c;
+  const int nblk = width > 0 ? tiles_r * a.tiles_c : 0;
   auto st = at::cuda::getCurrentCUDAStream();
-  const bool vec = a.vec_ok && (a.C % 8 == 0) && (a.r0 % 8 == 0) && (a.r1 % 8 == 0 || a.r1 == a.R) && (a.R % 8 == 0);
+  const bool vec = vec_shape_ok(a);
   int grid_x = nblk;
   if (vec && !a.transpose) {
-    a.tiles_c = a.Mp / 128;
-    grid_x = rows > 0 ? ((rows + 15) / 16) * a.tiles_c : 0;
+    a.tiles_c = (width + 127) / 128;
+    grid_x = rows > 0 && width > 0 ? ((rows + 15) / 16) * a.tiles_c : 0;
   }
   auto partial = at::zeros({B, std::max(grid_x, 1)}, meta_i64.options().dtype(at::kFloat));
   a.partial = partial.data_ptr<float>();
@@ -474,13 +488,14 @@ void dist_apply(const at::Tensor& meta_i64, const at::Tensor& meta_i32, const at
   const at::cuda::CUDAGuard guard(meta_i64.device());
   DistArgs a = make_args(meta_i64, meta_i32, peer_base, ints, floats, false, has_var);
   const int B = meta_i64.size(1);
-  a.tiles_c = (a.C + T - 1) / T;
+  const int width = a.c1 - a.c0;
+  a.tiles_c = (width + T - 1) / T;
   const int rows = a.r1 - a.r0;
-  if (rows <= 0) return;
+  if (rows <= 0 || width <= 0) return;
   auto st = at::cuda::getCurrentCUDAStream();
-  const bool vec = a.vec_ok && (a.C % 8 == 0) && (a.r0 % 8 == 0) && (a.r1 % 8 == 0 || a.r1 == a.R) && (a.R % 8 == 0);
+  const bool vec = vec_shape_ok(a);
   if (vec && !a.transpose) {
-    a.tiles_c = (a.C + 127) / 128;
+    a.tiles_c = (width + 127) / 128;
     dist_apply_rows_vec<<<dim3(((rows + 15) / 16) * a.tiles_c, B), NT, 0, st>>>(a);
   } else if (vec) {
     dist_apply_tr_vec<<<dim3(((rows + T - 1) / T) * a.tiles_c, B), NT, 0, st>>>(a);
@@ -528,6 +543,26 @@ __global__ void push_slots_kernel(const uint4* __restrict__ src, const int64_t* 
   for (; i < slot_vec; i += stride) dst[i] = s[i];
 }
 
+// For every rank k: out[k * slot + i] = peer_k[off + k * slot + i] (k == rank reads
+// its own staging). The all-gather by pulls: each rank has put its shard into its
+// own slot; the result lands straight in the caller's output with no staging copy.
+__global__ void pull_slots_kernel(uint4* __restrict__ out, const int64_t* peer_base, long long off, long long slot_vec,
+                                  int rank, int world) {
+  const int k = (blockIdx.y + rank) % world;
+  const uint4* src = reinterpret_cast<const uint4*>(peer_base[k] + off) + (long long)k * slot_vec;
+  uint4* dst = out + (long long)k * slot_vec;
+  const long long stride = (long long)gridDim.x * blockDim.x;
+  long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+  for (; i + 3 * stride < slot_vec; i += 4 * stride) {
+    const uint4 a = src[i], b = src[i + stride], c = src[i + 2 * stride], d = src[i + 3 * stride];
+    dst[i] = a;
+    dst[i + stride] = b;
+    dst[i + 2 * stride] = c;
+    dst[i + 3 * stride] = d;
+  }
+  for (; i < slot_vec; i += stride) dst[i] = src[i];
+}
+
 // out[i] = scale * sum_j staging[j * n + i] (local), dt 0 fp32 / 1 bf16.
 __global__ void local_slot_sum_kernel(void* __restrict__ out, const void* __restrict__ staging, long long n, int world,
                                       int dt, float scale) {
@@ -559,6 +594,20 @@ void push_slots(const at::Tensor& src, const at::Tensor& peer_base, int64_t off,
   push_slots_kernel<<<dim3(per, (unsigned)world), 256, 0, at::cuda::getCurrentCUDAStream()>>>(
       reinterpret_cast<const uint4*>(src.data_ptr()), peer_base.data_ptr<int64_t>(), off, slot_vec, (int)rank,
       (int)world, per_peer ? 1 : 0);
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+void pull_slots(at::Tensor& out, const at::Tensor& peer_base, int64_t off, int64_t slot_bytes, int64_t rank,
+                int64_t world, int64_t max_ctas) {
+  const at::cuda::CUDAGuard guard(out.device());
+  TORCH_CHECK(out.is_contiguous() && slot_bytes % 16 == 0 && off % 16 == 0 &&
+              reinterpret_cast<uintptr_t>(out.data_ptr()) % 16 == 0);
+  TORCH_CHECK(out.numel() * out.element_size() == slot_bytes * world);
+  const long long slot_vec = slot_bytes / 16;
+  if (slot_vec == 0) return;
+  const int per = (int)std::max<long long>(1, std::min<long long>(max_ctas / world, (slot_vec + 1023) / 1024));
+  pull_slots_kernel<<<dim3(per, (unsigned)world), 256, 0, at::cuda::getCurrentCUDAStream()>>>(
+      reinterpret_cast<uint4*>(out.data_ptr()), peer_base.data_ptr<int64_t>(), off, slot_vec, (int)rank, (int)world);
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 

@@ -70,7 +70,7 @@ struct PackArgs {
   int R, C;            // logical (param-oriented) matrix shape
   long long ld;        // row stride of each source/buffer matrix, elements
   int transpose;       // workspace holds src^T
-  int Np, Mp;          // workspace rows / cols (multiples of 256)
+  int Np, Mp;          // workspace rows / cols (multiples of TILE = 64; the GEMM layouts use 256)
   float momentum;
   int nesterov, maximize;
   __nv_bfloat16* out;  // [B, Np, Mp]
@@ -660,6 +660,9 @@ extern "C" int dmb_pack_normalize_noalloc(const void* src, int src_dtype, int ba
   const int64_t esize = src_dtype == 0 ? 4 : 2;
   noalloc_fill_ptrs<<<(batch + 255) / 256, 256, 0, stream>>>(reinterpret_cast<int64_t>(src), (int64_t)R * C * esize,
                                                               batch);
+  // Peek (not Get) after every launch: the error state is left as found, and the
+  // first failure is returned before a later kernel could read what it missed.
+  if ((e = cudaPeekAtLastError()) != cudaSuccess) return (int)e;
   PackArgs a{};
   a.src = ptrs;
   a.buf = nullptr;
@@ -677,7 +680,8 @@ extern "C" int dmb_pack_normalize_noalloc(const void* src, int src_dtype, int ba
   a.partial = partial;
   a.tiles_c = Mp / TILE;
   muon_pack_kernel<<<dim3((unsigned)tiles, batch), PACK_THREADS, 0, stream>>>(a);
+  if ((e = cudaPeekAtLastError()) != cudaSuccess) return (int)e;
   norm_finalize_kernel<<<batch, 256, 0, stream>>>(partial, (int)tiles, fac, eps, inv_norm, nullptr);
-  return (int)cudaGetLastError();
+  return (int)cudaPeekAtLastError();
 }
 

@@ -45,7 +45,9 @@ enum {
 //            zero-padded bf16 copy.
 // inv_norm:  fp32 [batch]; receives 1 / (||X_b||_F * fac + eps).
 // Returns 0 on success, a cudaError_t value from set-up or launch, or -1 for
-// arguments outside the documented limits.
+// arguments outside the documented limits. Launch errors are read with
+// cudaPeekAtLastError, so the thread's error state is left untouched, and a
+// nonzero value may be an earlier, still pending error of the caller's own.
 int dmb_pack_normalize_noalloc(const void* src, int src_dtype, int batch, int R, int C, int Np, int Mp,
                                float fac, float eps, void* out_ws, float* inv_norm, cudaStream_t stream);
 

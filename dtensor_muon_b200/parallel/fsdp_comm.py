@@ -4,9 +4,10 @@ FSDP2 (``torch.distributed.fsdp.fully_shard``) keeps its scheduling (prefetch,
 streams, copy-in / copy-out); only the two collectives are replaced, through
 ``FSDPModule.set_custom_all_gather`` / ``set_custom_reduce_scatter``:
 
-* all-gather: ``push_slots`` stores this rank's shard into slot ``rank`` of
-  every rank's symmetric staging (posted NVLink stores), one bounded device
-  barrier, then a local copy of the W slots into FSDP's output.
+* all-gather (default, pull): this rank's shard goes into slot ``rank`` of its
+  own symmetric staging, one bounded device barrier, then ``pull_slots`` loads
+  every peer's slot over NVLink straight into FSDP's output. (Push variant:
+  ``push_slots`` stores the shard into every peer's staging, barrier, local copy.)
 * reduce-scatter: ``push_slots`` stores chunk ``k`` of the local gradient into
   slot ``rank`` of rank k's staging, one barrier, then ``local_slot_sum`` adds
   the W slots in fp32 (one bf16 rounding instead of one per hop).
@@ -39,9 +40,11 @@ def _ws(group, device, purpose):
 class _PushStaging:
     """Double-buffered staging in one symmetric buffer: call i uses half i % 2.
 
-    A call pushes into every peer's current half, passes one barrier and then
-    reads only its own half. The barrier of call i + 1 orders every rank's
-    reads of half i % 2 (call i) before anyone pushes into it again (call i + 2).
+    A push call stores into every peer's current half, passes one barrier and
+    then reads only its own half; a pull call writes only its own slot of its
+    own half, passes the barrier and reads every peer's half. Either way the
+    barrier of call i + 1 orders every rank's reads of half i % 2 (call i)
+    before anyone writes into it again (call i + 2).
     """
 
     def __init__(self, purpose: str):
@@ -67,8 +70,16 @@ def _staging(purpose: str) -> _PushStaging:
     return _STAGING[purpose]
 
 
+# All-gather scheme: "pull" (default) copies this rank's shard into its own
+# staging slot, passes one barrier and pulls every slot straight into FSDP's
+# output (P2P loads); "push" stores the shard into every peer's staging, passes
+# the barrier and copies the W slots into the output locally (one extra
+# full-size local copy).
+AG_MODE = os.environ.get("DMB_AG_MODE", "pull")
+
+
 class P2PAllGather(AllGather):
-    """All-gather by P2P stores: shard -> slot ``rank`` of every peer's staging."""
+    """All-gather over peer memory (see ``AG_MODE``)."""
 
     def __init__(self):
         self._stage = _staging("fsdp_ag")
@@ -83,6 +94,12 @@ class P2PAllGather(AllGather):
         world = dist.get_world_size(group)
         ws, buf, peers, off = self._stage.half(group, output_tensor.device, nbytes * world)
         C = _ext.load()
+        if AG_MODE == "pull":
+            mine = off + ws.rank * nbytes
+            buf[mine : mine + nbytes].copy_(input_tensor.view(-1).view(torch.uint8))
+            ws.barrier()  # every rank's shard is in its own staging slot
+            C.pull_slots(output_tensor.view(-1), peers, off, nbytes, ws.rank, world, COMM_CTAS)
+            return None
         C.push_slots(input_tensor, peers, off, nbytes, ws.rank, world, False, COMM_CTAS)
         ws.barrier()  # every shard has landed in every rank's staging
         output_tensor.view(-1).view(torch.uint8).copy_(buf[off : off + nbytes * world])

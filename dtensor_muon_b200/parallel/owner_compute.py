@@ -21,7 +21,7 @@ from dataclasses import dataclass
 
 import torch
 from torch import Tensor
-from torch.distributed.tensor import DTensor, Shard
+from torch.distributed.tensor import DTensor, Replicate, Shard
 
 from ..ops import _ext
 from ..ops.ortho import WORKSPACE, coefficient_table, dtype_code, layout_for, norm_factor
@@ -37,24 +37,98 @@ def _rows(R: int, world: int, rank: int) -> tuple[int, int]:
     return min(rank * chunk, R), min((rank + 1) * chunk, R)
 
 
+def shard_dim(placements) -> int | None:
+    """Mesh dim that shards tensor dim 0 when every other mesh dim replicates
+    (FSDP: ``(Shard(0),)``; HSDP: ``(Replicate(), Shard(0))``), else None."""
+    dims = [i for i, pl in enumerate(placements) if pl == Shard(0)]
+    if len(dims) != 1 or any(pl != Replicate() for i, pl in enumerate(placements) if i != dims[0]):
+        return None
+    return dims[0]
+
+
+@dataclass(frozen=True)
+class ShardLayout:
+    """Where this rank's local shard sits in the global matrix, and the group of
+    ranks that together hold every block of it (owner compute runs over that group).
+
+    * FSDP ``(Shard(0),)`` / HSDP ``(Replicate(), Shard(0))``: row blocks over the
+      shard dim's group; the replicas of an HSDP mesh each run their own group.
+    * FSDP x TP ``(_StridedShard(0) | Shard(0), Shard(0) | Shard(1))`` on a mesh
+      that spans the whole job: every rank holds one rectangle (a row block of a
+      column-parallel weight, or a row x column block of a row-parallel one),
+      and the group is the whole job.
+    """
+
+    group: object
+    world: int
+    rank: int
+    r0: int
+    r1: int
+    c0: int
+    c1: int
+
+
+def _is_shard(pl) -> bool:
+    from torch.distributed.tensor.placement_types import _StridedShard
+
+    return isinstance(pl, (Shard, _StridedShard))
+
+
+def shard_layout(t: DTensor) -> ShardLayout | None:
+    import torch.distributed as dist
+    from torch.distributed.tensor._utils import compute_local_shape_and_global_offset
+
+    mesh, pls = t.device_mesh, tuple(t.placements)
+    if t.ndim != 2:
+        return None
+    d = shard_dim(pls)
+    R, C = t.shape
+    if d is not None and type(pls[d]) is Shard:
+        world, rank = mesh.size(d), mesh.get_local_rank(d)
+        r0, r1 = _rows(R, world, rank)
+        return ShardLayout(mesh.get_group(d), world, rank, r0, r1, 0, C)
+    if not all(_is_shard(pl) and pl.dim in (0, 1) for pl in pls) or mesh.size() != dist.get_world_size():
+        return None
+    shape, off = compute_local_shape_and_global_offset(t.shape, mesh, pls)
+    r0, c0 = int(off[0]), int(off[1])
+    return ShardLayout(dist.group.WORLD, dist.get_world_size(), dist.get_rank(), r0, r0 + int(shape[0]), c0,
+                       c0 + int(shape[1]))
+
+
 def eligible(params: list[Tensor], grads: list[Tensor], buffers: list[Tensor], variances=None) -> bool:
+    """2-D DTensors whose local shards are rectangles of the global matrix
+    (:class:`ShardLayout`). With replica dims (HSDP) each replica group runs owner
+    compute over its own shard group; the replicas hold identical gradients (FSDP
+    reduced them across replicas), so they compute identical updates, as the
+    reference's stack + redistribute does (src/muonium/orthogonalize/orthogonalize.py:140-155)."""
     if not params or not symm.available():
         return False
     g0 = grads[0]
     if not isinstance(g0, DTensor) or g0.ndim != 2:
         return False
     mesh = g0.device_mesh
-    if mesh.ndim != 1 or tuple(g0.placements) != (Shard(0),) or mesh.device_type != "cuda":
+    pls = tuple(g0.placements)
+    if mesh.device_type != "cuda":
         return False
-    world, rank = mesh.size(), mesh.get_local_rank()
-    r0, r1 = _rows(g0.shape[0], world, rank)
-    tensors = list(params) + list(grads) + list(buffers) + (list(variances) if variances is not None else [])
+    lay = shard_layout(g0)
+    if lay is None:
+        return False
+    shape = (lay.r1 - lay.r0, lay.c1 - lay.c0)
+    tensors = list(params) + list(grads) + list(buffers)
     for t in tensors:
-        if not isinstance(t, DTensor) or t.device_mesh != mesh or tuple(t.placements) != (Shard(0),):
+        if not isinstance(t, DTensor) or t.device_mesh != mesh or tuple(t.placements) != pls:
             return False
         loc = t.to_local()
-        if not loc.is_cuda or not loc.is_contiguous() or loc.shape[0] != r1 - r0:
+        if not loc.is_cuda or not loc.is_contiguous() or tuple(loc.shape) != shape:
             return False
+    if variances is not None:
+        # NorMuon's per-row variance: one value per global row, sharded like the rows
+        for v in variances:
+            if not isinstance(v, DTensor) or v.device_mesh != mesh:
+                return False
+            loc = v.to_local()
+            if not loc.is_cuda or not loc.is_contiguous() or loc.numel() != lay.r1 - lay.r0:
+                return False
     for p, g, b in zip(params, grads, buffers, strict=True):
         if p.shape != g.shape or b.shape != g.shape or b.dtype != torch.float32:
             return False
@@ -87,16 +161,16 @@ def owner_compute_update(
 ) -> None:
     """``momentum_done``: the grads already hold g' (momentum updated in the
     FSDP reduce-scatter), so the pack only casts and scatters them."""
-    mesh = grads[0].device_mesh
-    world, rank = mesh.size(), mesh.get_local_rank()
+    sl = shard_layout(grads[0])
+    world, rank = sl.world, sl.rank
     R, C = grads[0].shape
     lay = layout_for(R, C)
-    r0, r1 = _rows(R, world, rank)
     device = grads[0].to_local().device
-    ws = symm.workspace_for(mesh.get_group(), device)
+    ws = symm.workspace_for(sl.group, device)
+    rpad, cpad = (lay.Mp, lay.Np) if lay.transpose else (lay.Np, lay.Mp)
     grp = _Group(
-        C_=_ext.load(), lay=lay, R=R, C=C, rank=rank, world=world, r0=r0, r1=r1,
-        g1=(lay.Mp if lay.transpose else lay.Np) if rank == world - 1 else r1,
+        C_=_ext.load(), lay=lay, R=R, C=C, rank=rank, world=world, r0=sl.r0, r1=sl.r1,
+        g1=rpad if sl.r1 == R else sl.r1, c0=sl.c0, c1=sl.c1, h1=cpad if sl.c1 == C else sl.c1,
         coeffs=coefficient_table(strategy, ns_steps), fac=norm_factor(strategy), eps=eps,
         weight_decay=weight_decay, cautious_wd=cautious_wd, momentum=momentum, nesterov=nesterov,
         maximize=maximize, muon_beta2=muon_beta2, has_var=variances is not None, device=device,
@@ -174,6 +248,9 @@ class _Group:
     r0: int
     r1: int
     g1: int
+    c0: int
+    c1: int
+    h1: int
     coeffs: Tensor
     fac: float
     eps: float
@@ -228,7 +305,7 @@ class _Spec:
             x_off, res_off, base + self.sums_rel, base + self.vbuf_rel, base + self.rs_rel,
             g.gdt, g.pdt, g.R, g.C, int(lay.transpose), lay.Np, lay.Mp, g.r0, g.r1, g.g1, g.rank, g.world,
             int(g.nesterov), 0 if g.momentum_done else int(g.maximize), int(g.cautious_wd), int(g.has_var),
-            self.vec_ok,
+            self.vec_ok, g.c0, g.c1, g.h1, g.c1 - g.c0,
         ]
 
     def pack(self, peer_base):

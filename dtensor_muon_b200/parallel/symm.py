@@ -46,6 +46,9 @@ class SymmetricWorkspace:
         self.rank = dist.get_rank(group)
         self.world = dist.get_world_size(group)
         name = group.group_name
+        enable = getattr(symm_mem, "enable_symm_mem_for_group", None)
+        if enable is not None:  # subgroups (HSDP shard groups, TP/EP groups) need their own store
+            enable(name)
         self._flags = symm_mem.empty(max(64, self.world), dtype=torch.int32, device=device)
         self._flags.zero_()
         hdl = symm_mem.rendezvous(self._flags, name)

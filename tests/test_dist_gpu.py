@@ -12,21 +12,25 @@ pytestmark = [pytest.mark.gpu, pytest.mark.multigpu]
 SHAPES = [(256, 512), (512, 256), (200, 384), (384, 200), (64, 96), (1024, 4096)]
 
 
-def _worker(rank, world, algorithm, strategy, n_steps, dtype_name):
+def _worker(rank, world, algorithm, strategy, n_steps, dtype_name, mesh_shape=None, placements=None):
     import torch
     from torch.distributed.device_mesh import init_device_mesh
-    from torch.distributed.tensor import Shard, distribute_tensor
+    from torch.distributed.tensor import Replicate, Shard, distribute_tensor
 
     from dtensor_muon_b200 import Muon
     from dtensor_muon_b200.ops import _ext
 
     dtype = getattr(torch, dtype_name)
     device = torch.device("cuda", rank)
-    mesh = init_device_mesh("cuda", (world,))
+    mesh = init_device_mesh("cuda", tuple(mesh_shape) if mesh_shape else (world,))
+    # FSDP: (Shard(0),); HSDP: (Replicate(), Shard(0)) over a (replicas, shards) mesh
+    pl = [Shard(0)] if mesh.ndim == 1 else [Replicate(), Shard(0)]
+    if placements is not None:  # e.g. "S1" (row-parallel TP) or "S0,S1" (FSDP x row-parallel TP)
+        pl = [Shard(int(x[1])) if x[0] == "S" else Replicate() for x in placements.split(",")]
     gen = torch.Generator().manual_seed(0)
     fulls = [torch.randn(s, generator=gen).to(dtype) for s in SHAPES for _ in range(3)]
     ref_params = [torch.nn.Parameter(f.clone().to(device)) for f in fulls]
-    dist_params = [torch.nn.Parameter(distribute_tensor(f.clone().to(device), mesh, [Shard(0)])) for f in fulls]
+    dist_params = [torch.nn.Parameter(distribute_tensor(f.clone().to(device), mesh, pl)) for f in fulls]
     kw = dict(lr=0.05, wd=0.1, orthogonalization_strategy=strategy)
     ref = Muon([{"params": ref_params, "algorithm": algorithm}], foreach=True, **kw)
     opt = Muon([{"params": dist_params, "algorithm": algorithm}], foreach=True, **kw)
@@ -35,7 +39,7 @@ def _worker(rank, world, algorithm, strategy, n_steps, dtype_name):
         for p, g in zip(ref_params, grads):
             p.grad = g.to(device)
         for p, g in zip(dist_params, grads):
-            p.grad = distribute_tensor(g.to(device), mesh, [Shard(0)])
+            p.grad = distribute_tensor(g.to(device), mesh, pl)
         ref.step()
         opt.step()
     torch.cuda.synchronize()
@@ -60,3 +64,57 @@ def test_owner_compute_matches_single_process(algorithm, strategy):
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
 def test_owner_compute_bf16_params():
     run_distributed(_worker, 2, args=("muon", "polar_express", 2, "bfloat16"), backend="nccl", device_type="cuda")
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+def test_owner_compute_hsdp_mesh_matches_single_process():
+    """HSDP placements (Replicate(), Shard(0)) on a (1, 2) mesh take the fused
+    owner-compute path (one shard group) and match the single-process step."""
+    run_distributed(_hsdp_worker, 2, args=((1, 2),), backend="nccl", device_type="cuda", timeout_s=120)
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 4, reason="needs 4 GPUs")
+def test_owner_compute_hsdp_2x2_matches_single_process():
+    run_distributed(_hsdp_worker, 4, args=((2, 2),), backend="nccl", device_type="cuda", timeout_s=180)
+
+
+def _hsdp_worker(rank, world, mesh_shape):
+    from dtensor_muon_b200.parallel import owner_compute
+
+    calls = []
+    orig = owner_compute.owner_compute_update
+    owner_compute.owner_compute_update = lambda *a, **k: (calls.append(1), orig(*a, **k))[1]
+    try:
+        _worker(rank, world, "muon", "polar_express", 2, "float32", mesh_shape)
+    finally:
+        owner_compute.owner_compute_update = orig
+    assert calls, "HSDP batches must take the owner-compute path"
+
+
+def _rect_worker(rank, world, mesh_shape, placements, algorithm):
+    from dtensor_muon_b200.parallel import owner_compute
+
+    calls = []
+    orig = owner_compute.owner_compute_update
+    owner_compute.owner_compute_update = lambda *a, **k: (calls.append(1), orig(*a, **k))[1]
+    try:
+        _worker(rank, world, algorithm, "newton_schulz", 2, "float32", mesh_shape, placements)
+    finally:
+        owner_compute.owner_compute_update = orig
+    assert calls, "column-sharded batches must take the owner-compute path"
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+@pytest.mark.parametrize("algorithm", ["muon", "normuon"])
+def test_owner_compute_column_shards_match_single_process(algorithm):
+    """Row-parallel TP placement (Shard(1)): every rank holds a column block; owner
+    compute packs and applies rectangles."""
+    run_distributed(_rect_worker, 2, args=((2,), "S1", algorithm), backend="nccl", device_type="cuda",
+                    timeout_s=120)
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 4, reason="needs 4 GPUs")
+def test_owner_compute_2d_rectangles_match_single_process():
+    """FSDP x row-parallel TP on a (2, 2) mesh: row x column blocks."""
+    run_distributed(_rect_worker, 4, args=((2, 2), "S0,S1", "muon"), backend="nccl", device_type="cuda",
+                    timeout_s=180)

@@ -9,13 +9,16 @@ from testkit import run_distributed
 pytestmark = [pytest.mark.gpu, pytest.mark.multigpu]
 
 
-def _worker(rank, world):
+def _worker(rank, world, ag_mode="pull"):
     import torch
     from torch.distributed.device_mesh import init_device_mesh
 
     from dtensor_muon_b200.models.llama import lm_loss, preset
     from dtensor_muon_b200.ops import _ext
+    from dtensor_muon_b200.parallel import fsdp_comm
     from dtensor_muon_b200.train import build_llama, build_optimizer
+
+    fsdp_comm.AG_MODE = ag_mode
 
     mesh = init_device_mesh("cuda", (world,))
     cfg = preset("tiny", vocab_size=1024, dim=256, n_layers=2)
@@ -48,5 +51,6 @@ def _worker(rank, world):
 
 
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
-def test_fsdp_p2p_collectives_match_nccl():
-    run_distributed(_worker, 2, backend="nccl", device_type="cuda")
+@pytest.mark.parametrize("ag_mode", ["pull", "push"])
+def test_fsdp_p2p_collectives_match_nccl(ag_mode):
+    run_distributed(_worker, 2, args=(ag_mode,), backend="nccl", device_type="cuda")

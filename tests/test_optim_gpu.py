@@ -239,3 +239,26 @@ def test_fused_adam_group_keeps_step_on_device_and_matches_torch():
         ref.step()
     assert opt.state[a[0]]["step"].device == a[0].device
     torch.testing.assert_close(a[0], b[0])
+
+
+@pytest.mark.parametrize("n", [4096, 4099])
+def test_native_adamw_edge_values_match_torch(n):
+    """Zero gradients, tiny gradients (subnormal second moment) and one huge
+    gradient element (second moment overflows to +inf) on the vector (n % 8 == 0)
+    and scalar paths: same results as torch.optim.AdamW, no NaN introduced."""
+    g = torch.zeros(n)
+    g[: n // 4] = 1e-20  # g^2 ~ 1e-40: subnormal fp32
+    g[n // 4 : n // 2] = torch.randn(n // 4, generator=torch.Generator().manual_seed(4))
+    g[7] = 1e20  # g^2 overflows to inf
+    a = nn.Parameter(torch.randn(n, generator=torch.Generator().manual_seed(5)).cuda())
+    b = nn.Parameter(a.detach().clone())
+    opt = Muon([{"params": [a], "algorithm": "adamw", "lr": 0.01, "wd": 0.1}])
+    ref = torch.optim.AdamW([b], lr=0.01, weight_decay=0.1, betas=(0.9, 0.95), foreach=False)
+    for _ in range(2):
+        a.grad, b.grad = g.cuda(), g.cuda()
+        opt.step()
+        ref.step()
+    assert torch.isfinite(a).all()
+    torch.testing.assert_close(a, b, rtol=1e-5, atol=1e-6)
+    # subnormal second moments carry few significant bits: compare them absolutely
+    torch.testing.assert_close(opt.state[a]["exp_avg_sq"], ref.state[b]["exp_avg_sq"], rtol=1e-5, atol=1e-38)

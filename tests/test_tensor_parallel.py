@@ -124,3 +124,47 @@ def _fsdp_tp_worker(rank, world):
 
 def test_fsdp_x_tp_normuon_gloo_four_ranks():
     run_distributed(_fsdp_tp_worker, 4)
+
+
+def _layout_worker(rank, world):
+    import torch
+    import torch.distributed as dist
+    from torch.distributed.device_mesh import init_device_mesh
+
+    from dtensor_muon_b200.models.llama import Llama, preset
+    from dtensor_muon_b200.parallel.owner_compute import shard_layout
+    from dtensor_muon_b200.parallel.tensor_parallel import apply_fsdp_tp
+
+    cfg = preset("tiny")
+    torch.manual_seed(0)
+    model = Llama(cfg)
+    model.init_weights(seed=0)
+    mesh = init_device_mesh("cpu", (2, 2), mesh_dim_names=("dp", "tp"))
+    apply_fsdp_tp(model, mesh)
+    seen = 0
+    for name, p in model.named_parameters():
+        if p.ndim != 2 or "layers." not in name:
+            continue
+        lay = shard_layout(p)
+        assert lay is not None, (name, p.placements)
+        assert lay.world == world and lay.rank == rank
+        local = p.to_local()
+        full = p.full_tensor()
+        assert tuple(local.shape) == (lay.r1 - lay.r0, lay.c1 - lay.c0), (name, local.shape, lay)
+        torch.testing.assert_close(local, full[lay.r0 : lay.r1, lay.c0 : lay.c1])
+        # the rectangles of all ranks tile the matrix exactly once
+        rect = torch.tensor([lay.r0, lay.r1, lay.c0, lay.c1])
+        rects = [torch.zeros_like(rect) for _ in range(world)]
+        dist.all_gather(rects, rect)
+        cover = torch.zeros(p.shape, dtype=torch.int32)
+        for r0, r1, c0, c1 in (x.tolist() for x in rects):
+            cover[r0:r1, c0:c1] += 1
+        assert torch.all(cover == 1), name
+        seen += 1
+    assert seen >= 7 * cfg.n_layers
+
+
+def test_fsdp_x_tp_shards_are_rectangles_tiling_each_matrix_gloo():
+    """Owner compute's layout of FSDP x TP shards (strided row blocks of column-parallel
+    weights, row x column blocks of row-parallel ones) on a (2, 2) mesh."""
+    run_distributed(_layout_worker, 4)
