@@ -33,50 +33,55 @@ from . import symm
 
 
 class _Plan:
-    """Destination of every (sorted) source row and the local receive layout."""
+    """Destination of every (sorted) source row and the local receive layout.
 
-    def __init__(self, counts_all: Tensor, rank: int, world: int, n_experts: int):
-        # counts_all: CPU int64 [W, E] = rows source rank s sends to expert e
+    Built from the [W, E] count matrix with vectorised tensor ops on the
+    tokens' device: per-row destinations (rank, row) and the NCCL receive
+    permutation never pass through Python loops. The only host transfer is the
+    W x E count matrix itself (one small copy per layer), which sizes the
+    receive buffers and the expert GEMMs.
+    """
+
+    def __init__(self, counts_all: Tensor, sorted_experts: Tensor, rank: int, world: int, n_experts: int):
+        # counts_all: int64 [W, E] on the device = rows source rank s sends to expert e
+        # sorted_experts: this rank's expert id per sorted row (ascending)
         self.world, self.rank = world, rank
         el = n_experts // world
         self.local_experts = el
-        # receive offsets: owner d, local expert e, source s -> row
-        off = torch.zeros(world, n_experts, dtype=torch.int64)
-        for d in range(world):
-            cur = 0
-            for e in range(d * el, (d + 1) * el):
-                for s in range(world):
-                    off[s, e] = cur
-                    cur += int(counts_all[s, e])
-        self.recv_rows = [int(counts_all[:, d * el:(d + 1) * el].sum()) for d in range(world)]
-        mine = counts_all[rank]  # rows I send per expert, in expert order (rows are pre-sorted)
-        dst_rank, dst_row = [], []
-        for e in range(n_experts):
-            n = int(mine[e])
-            if n:
-                dst_rank += [e // el] * n
-                base = int(off[rank, e])
-                dst_row += list(range(base, base + n))
-        self.dst_rank = torch.tensor(dst_rank, dtype=torch.int32)
-        self.dst_row = torch.tensor(dst_row, dtype=torch.int32)
-        self.local_counts = counts_all[:, rank * el:(rank + 1) * el].sum(0)  # per local expert
-        self.send_split = [int(mine[d * el:(d + 1) * el].sum()) for d in range(world)]
-        self.recv_split = [int(counts_all[s, rank * el:(rank + 1) * el].sum()) for s in range(world)]
-        # NCCL receive order is (source, local expert); permutation to (local expert, source)
-        perm = []
-        src_base = torch.tensor([0] + self.recv_split).cumsum(0)
-        for e in range(el):
-            for s in range(world):
-                n = int(counts_all[s, rank * el + e])
-                start = int(src_base[s]) + int(counts_all[s, rank * el:rank * el + e].sum())
-                perm += list(range(start, start + n))
-        self.nccl_perm = torch.tensor(perm, dtype=torch.int64)
+        dev = counts_all.device
+        # Receive layout of owner d: (local expert, source) blocks in order.
+        # off[s, e] = rows of owner(e) before block (e, s).
+        blocks = counts_all.t().reshape(world, el, world)  # [owner, local e, source]
+        flat = blocks.reshape(world, el * world)
+        before = torch.cumsum(flat, dim=1) - flat  # exclusive, within owner
+        off = before.reshape(world, el, world).permute(2, 0, 1).reshape(world, n_experts)  # [s, e]
+        # Destination of each of my sorted rows: owner of its expert, off + rank within its expert run
+        mine = counts_all[rank]
+        start = torch.cumsum(mine, 0) - mine
+        e = sorted_experts.long()
+        pos = torch.arange(e.numel(), device=dev)
+        self.dst_rank_d = (e // el).to(torch.int32)
+        self.dst_row_d = (off[rank].index_select(0, e) + pos - start.index_select(0, e)).to(torch.int32)
+        # Host-side sizes: one [W, E] copy.
+        host = counts_all.cpu()
+        self.recv_rows = host.t().reshape(world, el * world).sum(1).tolist()
+        self.local_counts = host[:, rank * el:(rank + 1) * el].sum(0)  # per local expert
+        self.send_split = host[rank].reshape(world, el).sum(1).tolist()
+        self.recv_split = host[:, rank * el:(rank + 1) * el].sum(1).tolist()
+        # NCCL receives (source, local expert) blocks; permutation to (local expert, source).
+        c_se = counts_all[:, rank * el:(rank + 1) * el]  # [s, e_local]
+        old_start = (torch.cumsum(c_se.reshape(-1), 0) - c_se.reshape(-1)).reshape(world, el)
+        c_es = c_se.t().reshape(-1)  # blocks in (e, s) order
+        new_start = torch.cumsum(c_es, 0) - c_es
+        total = int(self.recv_rows[rank])
+        idx = torch.arange(total, device=dev)
+        blk_old = torch.repeat_interleave(old_start.t().reshape(-1), c_es, output_size=total)
+        blk_new = torch.repeat_interleave(new_start, c_es, output_size=total)
+        self.nccl_perm_d = blk_old + (idx - blk_new)
 
-    def to(self, device):
-        self.dst_rank_d = self.dst_rank.to(device, non_blocking=True)
-        self.dst_row_d = self.dst_row.to(device, non_blocking=True)
-        self.nccl_perm_d = self.nccl_perm.to(device, non_blocking=True)
-        return self
+    @property
+    def n_send(self) -> int:
+        return int(self.dst_rank_d.numel())
 
 
 class _P2PExchange:
@@ -102,7 +107,7 @@ class _P2PExchange:
         self.ws.barrier()
         region[: local.shape[0]].copy_(local)
         self.ws.barrier()  # every owner's results are in place
-        out = torch.empty(plan.dst_rank.numel(), local.shape[1], dtype=local.dtype, device=local.device)
+        out = torch.empty(plan.n_send, local.shape[1], dtype=local.dtype, device=local.device)
         C.ep_gather_rows(out, plan.dst_rank_d, plan.dst_row_d, peers, 0)
         return out
 
@@ -152,11 +157,12 @@ class ExpertParallel:
 
     def plan(self, expert_ids: Tensor) -> tuple[_Plan, Tensor, Tensor]:
         counts = torch.bincount(expert_ids, minlength=self.n_experts)
-        gathered = [torch.empty_like(counts) for _ in range(self.world)]
-        dist.all_gather(gathered, counts, group=self.group)
-        counts_all = torch.stack(gathered).cpu()
+        counts_all = torch.empty(self.world * self.n_experts, dtype=counts.dtype, device=counts.device)
+        dist.all_gather_into_tensor(counts_all, counts, group=self.group)
+        counts_all = counts_all.view(self.world, self.n_experts)
         order = torch.argsort(expert_ids, stable=True)
-        return _Plan(counts_all, self.rank, self.world, self.n_experts).to(expert_ids.device), order, counts
+        plan = _Plan(counts_all, expert_ids.index_select(0, order), self.rank, self.world, self.n_experts)
+        return plan, order, counts
 
     # -- transport: sorted source rows -> my expert-grouped rows, and back
     def _send(self, rows: Tensor, plan: _Plan) -> Tensor:

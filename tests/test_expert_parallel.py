@@ -84,3 +84,41 @@ def test_mixtral_single_gpu_step(opt_name):
     _ext.check_device_errors("cuda")
     assert torch.isfinite(loss)
     assert all(not torch.equal(b, p) for b, p in zip(before, experts))
+
+
+@pytest.mark.parametrize("world,n_experts,seed", [(2, 4, 0), (4, 8, 1), (8, 8, 2), (4, 16, 3)])
+def test_plan_matches_brute_force(world, n_experts, seed):
+    """The vectorised routing plan (device tensor ops) equals a per-row
+    construction: receive regions grouped by (local expert, source), each
+    source's rows of an expert contiguous, NCCL receive permutation."""
+    from dtensor_muon_b200.parallel.expert_parallel import _Plan
+
+    g = torch.Generator().manual_seed(seed)
+    counts_all = torch.randint(0, 5, (world, n_experts), generator=g)
+    counts_all[0, 0] = 0  # empty blocks
+    el = n_experts // world
+    for rank in range(world):
+        experts = torch.repeat_interleave(torch.arange(n_experts), counts_all[rank])
+        plan = _Plan(counts_all, experts, rank, world, n_experts)
+        # brute force: walk owners' layouts
+        off = {}
+        for d in range(world):
+            cur = 0
+            for e in range(d * el, (d + 1) * el):
+                for s in range(world):
+                    off[(s, e)] = cur
+                    cur += int(counts_all[s, e])
+        want_rank, want_row = [], []
+        for e in range(n_experts):
+            for j in range(int(counts_all[rank, e])):
+                want_rank.append(e // el)
+                want_row.append(off[(rank, e)] + j)
+        assert plan.dst_rank_d.tolist() == want_rank
+        assert plan.dst_row_d.tolist() == want_row
+        assert plan.recv_rows == [int(counts_all[:, d * el:(d + 1) * el].sum()) for d in range(world)]
+        assert plan.send_split == [int(counts_all[rank, d * el:(d + 1) * el].sum()) for d in range(world)]
+        assert plan.recv_split == [int(counts_all[s, rank * el:(rank + 1) * el].sum()) for s in range(world)]
+        # NCCL order (source, local expert) -> (local expert, source)
+        labels = [(s, e) for s in range(world) for e in range(el) for _ in range(int(counts_all[s, rank * el + e]))]
+        permuted = [labels[i] for i in plan.nccl_perm_d.tolist()]
+        assert permuted == sorted(labels, key=lambda t: (t[1], t[0]))
