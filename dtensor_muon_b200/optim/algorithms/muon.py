@@ -31,7 +31,10 @@ def fused_path_ok(params, grads, buffers, split_sizes) -> bool:
 def distributed_fused(params, grads, buffers, lr_ratios, lr, split_sizes, ns_steps, kw, variances=None) -> bool:
     """Run the fused distributed path when the batch qualifies; returns whether it ran.
 
-    * 2-D FSDP (Shard(0)) DTensors: owner-compute over symmetric memory.
+    * 2-D row-sharded DTensors with fewer matrices than ranks: sharded
+      Newton-Schulz / Polar Express (:mod:`...parallel.sharded_ns`).
+    * other 2-D DTensors whose shards are rectangles (FSDP, HSDP, FSDP x TP):
+      owner compute over symmetric memory.
     * 3-D DTensors sharded only on dim 0: the local shards are whole matrices,
       so the single-GPU fused kernels run on them with no communication.
     """
@@ -45,6 +48,20 @@ def distributed_fused(params, grads, buffers, lr_ratios, lr, split_sizes, ns_ste
 
     effs = lr_effs(lr, lr_ratios)
     fused = [id(p) in FUSED_GRADS for p in params]
+    from ...parallel import sharded_ns
+
+    if sharded_ns.eligible(params, grads, buffers, variances):
+        # Few matrices for many ranks: orthogonalise the row shards in place with
+        # an all-reduced partial Gram per iteration instead of idling owners.
+        for done in (False, True):
+            idx = [i for i, f in enumerate(fused) if f == done]
+            if idx:
+                sharded_ns.sharded_update(
+                    [params[i] for i in idx], [grads[i] for i in idx], [buffers[i] for i in idx],
+                    [effs[i] for i in idx], ns_steps=ns_steps, momentum_done=done, **kw,
+                )
+        FUSED_GRADS.difference_update(id(p) for p in params)
+        return True
     if owner_compute.eligible(params, grads, buffers, variances):
         # Grads whose momentum was applied inside the FSDP reduce-scatter hold g'.
         for done in (False, True):

@@ -118,3 +118,27 @@ def test_owner_compute_2d_rectangles_match_single_process():
     """FSDP x row-parallel TP on a (2, 2) mesh: row x column blocks."""
     run_distributed(_rect_worker, 4, args=((2, 2), "S0,S1", "muon"), backend="nccl", device_type="cuda",
                     timeout_s=180)
+
+
+def _sharded_worker(rank, world, strategy, dtype_name):
+    from dtensor_muon_b200.parallel import sharded_ns
+
+    calls = []
+    orig = sharded_ns.sharded_update
+    sharded_ns._FORCE = "1"
+    sharded_ns.sharded_update = lambda *a, **k: (calls.append(1), orig(*a, **k))[1]
+    try:
+        _worker(rank, world, "muon", strategy, 3, dtype_name)
+    finally:
+        sharded_ns.sharded_update = orig
+        sharded_ns._FORCE = None
+    assert calls, "tall row-sharded batches must take the sharded Newton-Schulz path"
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+@pytest.mark.parametrize("strategy", ["newton_schulz", "polar_express"])
+def test_sharded_newton_schulz_matches_single_process(strategy):
+    """Row shards orthogonalised in place with the all-reduced partial Gram
+    (tall shapes), against the single-process step."""
+    run_distributed(_sharded_worker, 2, args=(strategy, "float32"), backend="nccl", device_type="cuda",
+                    timeout_s=120)
