@@ -63,6 +63,8 @@ void push_slots(const at::Tensor& src, const at::Tensor& peer_base, int64_t off,
                 int64_t world, bool per_peer, int64_t max_ctas);
 void pull_slots(at::Tensor& out, const at::Tensor& peer_base, int64_t off, int64_t slot_bytes, int64_t rank,
                 int64_t world, int64_t max_ctas);
+void allreduce_inplace(const at::Tensor& peer_base, int64_t off, int64_t nbytes, int64_t dtype_code, int64_t rank,
+                       int64_t world, int64_t mc_base, int64_t max_ctas);
 void local_slot_sum(at::Tensor& out, const at::Tensor& staging_bytes, int64_t off, int64_t world, double scale,
                     int64_t max_ctas);
 void rs_sum_momentum(at::Tensor& out, const at::Tensor& staging_bytes, int64_t off, int64_t world, double scale,
@@ -137,6 +139,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("push_slots", &dmb::push_slots);
   m.def("local_slot_sum", &dmb::local_slot_sum);
   m.def("pull_slots", &dmb::pull_slots);
+  m.def("allreduce_inplace", &dmb::allreduce_inplace);
   m.def("rs_sum_momentum", &dmb::rs_sum_momentum);
   m.def("ep_scatter_rows", &dmb::ep_scatter_rows);
   m.def("ep_gather_rows", &dmb::ep_gather_rows);

@@ -563,6 +563,82 @@ __global__ void pull_slots_kernel(uint4* __restrict__ out, const int64_t* peer_b
   for (; i < slot_vec; i += stride) dst[i] = src[i];
 }
 
+// In-place all-reduce (sum) of n elements at byte offset `off` of every rank's
+// symmetric buffer. Rank r owns chunk r: it sums that chunk over all ranks and
+// writes the sum back into every rank's chunk. Two transports:
+//  * mc_base != 0 (NVLS): one multimem.ld_reduce through the NVSwitch
+//    multicast address returns the sum of all ranks' values, one multimem.st
+//    writes it to every rank (the switch reduces and replicates);
+//  * otherwise P2P: W 16-byte loads (one per peer), fp32 sum, W stores.
+// Callers put a device barrier before (inputs written) and after (results
+// visible). Elements are handled 8 (bf16) or 4 (fp32) at a time: 16 bytes.
+__device__ __forceinline__ void mm_ld_reduce_bf16x8(const void* mc, uint32_t (&r)[4]) {
+  asm volatile("multimem.ld_reduce.relaxed.sys.global.add.acc::f32.v4.bf16x2 {%0, %1, %2, %3}, [%4];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+               : "l"(mc)
+               : "memory");
+}
+__device__ __forceinline__ void mm_ld_reduce_f32x4(const void* mc, uint32_t (&r)[4]) {
+  asm volatile("multimem.ld_reduce.relaxed.sys.global.add.v4.f32 {%0, %1, %2, %3}, [%4];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+               : "l"(mc)
+               : "memory");
+}
+__device__ __forceinline__ void mm_st_16(void* mc, const uint32_t (&r)[4], int dt) {
+  if (dt == 0)
+    asm volatile("multimem.st.relaxed.sys.global.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(mc), "r"(r[0]), "r"(r[1]),
+                 "r"(r[2]), "r"(r[3])
+                 : "memory");
+  else
+    asm volatile("multimem.st.relaxed.sys.global.v4.bf16x2 [%0], {%1, %2, %3, %4};" ::"l"(mc), "r"(r[0]), "r"(r[1]),
+                 "r"(r[2]), "r"(r[3])
+                 : "memory");
+}
+
+__global__ void allreduce_inplace_kernel(const int64_t* peer_base, long long off, long long nvec, int dt, int rank,
+                                         int world, long long mc_base) {
+  // my chunk of 16-byte vectors
+  const long long per = (nvec + world - 1) / world;
+  const long long v0 = (long long)rank * per, v1 = min(nvec, v0 + per);
+  const long long stride = (long long)gridDim.x * blockDim.x;
+  for (long long v = v0 + (long long)blockIdx.x * blockDim.x + threadIdx.x; v < v1; v += stride) {
+    const long long byte = off + v * 16;
+    uint32_t r[4];
+    if (mc_base != 0) {
+      void* mc = reinterpret_cast<void*>(mc_base + byte);
+      if (dt == 0)
+        mm_ld_reduce_f32x4(mc, r);
+      else
+        mm_ld_reduce_bf16x8(mc, r);
+      mm_st_16(mc, r, dt);
+      continue;
+    }
+    float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+    for (int j = 0; j < world; ++j) {
+      const int k = (j + rank) % world;
+      const uint4 w = *reinterpret_cast<const uint4*>(peer_base[k] + byte);
+      const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
+      if (dt == 0) {
+#pragma unroll
+        for (int e = 0; e < 4; ++e) acc[e] += __uint_as_float(ws[e]);
+      } else {
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          acc[2 * e] += bf16_bits_to_float((uint16_t)(ws[e] & 0xFFFFu));
+          acc[2 * e + 1] += bf16_bits_to_float((uint16_t)(ws[e] >> 16));
+        }
+      }
+    }
+    uint4 out;
+    if (dt == 0)
+      out = make_uint4(__float_as_uint(acc[0]), __float_as_uint(acc[1]), __float_as_uint(acc[2]), __float_as_uint(acc[3]));
+    else
+      out = make_uint4(pack_bf16x2(acc[0], acc[1]), pack_bf16x2(acc[2], acc[3]), pack_bf16x2(acc[4], acc[5]),
+                       pack_bf16x2(acc[6], acc[7]));
+    for (int j = 0; j < world; ++j) *reinterpret_cast<uint4*>(peer_base[(j + rank) % world] + byte) = out;
+  }
+}
+
 // out[i] = scale * sum_j staging[j * n + i] (local), dt 0 fp32 / 1 bf16.
 __global__ void local_slot_sum_kernel(void* __restrict__ out, const void* __restrict__ staging, long long n, int world,
                                       int dt, float scale) {
@@ -608,6 +684,20 @@ void pull_slots(at::Tensor& out, const at::Tensor& peer_base, int64_t off, int64
   const int per = (int)std::max<long long>(1, std::min<long long>(max_ctas / world, (slot_vec + 1023) / 1024));
   pull_slots_kernel<<<dim3(per, (unsigned)world), 256, 0, at::cuda::getCurrentCUDAStream()>>>(
       reinterpret_cast<uint4*>(out.data_ptr()), peer_base.data_ptr<int64_t>(), off, slot_vec, (int)rank, (int)world);
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+void allreduce_inplace(const at::Tensor& peer_base, int64_t off, int64_t nbytes, int64_t dtype_code, int64_t rank,
+                       int64_t world, int64_t mc_base, int64_t max_ctas) {
+  const at::cuda::CUDAGuard guard(peer_base.device());
+  TORCH_CHECK(off % 16 == 0 && nbytes % 16 == 0 && (dtype_code == 0 || dtype_code == 1));
+  TORCH_CHECK(mc_base % 16 == 0);
+  const long long nvec = nbytes / 16;
+  if (nvec == 0) return;
+  const long long per = (nvec + world - 1) / world;
+  const int blocks = (int)std::max<long long>(1, std::min<long long>(max_ctas, (per + 255) / 256));
+  allreduce_inplace_kernel<<<blocks, 256, 0, at::cuda::getCurrentCUDAStream()>>>(
+      peer_base.data_ptr<int64_t>(), off, nvec, (int)dtype_code, (int)rank, (int)world, mc_base);
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 

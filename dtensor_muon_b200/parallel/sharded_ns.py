@@ -15,8 +15,9 @@ because X (X^T X)^k = (X X^T)^k X. With X's rows spread over the ranks,
 G = sum_r X_r^T X_r is a sum of per-rank partial Grams, so each iteration is:
 
     1. partial Gram of the local rows (tcgen05 kernel, epilogue-scaled on step 1)
-    2. all-reduce of G over the group: P2P push of the partial into every
-       peer's staging slot, one bounded device barrier, fp32 sum of the W slots
+    2. all-reduce of G over the group, in place in symmetric memory (the Gram
+       kernel writes its partial there): NVLS ``multimem`` reduce + broadcast
+       through the switch where multicast is available, else P2P loads/stores
     3. B = c G^2 + b G (every rank, replicated; C x C)
     4. X_r <- a X_r + X_r B on the local rows (tcgen05 kernel)
 
@@ -29,7 +30,6 @@ place. Per iteration a rank moves (W - 1) C^2 bf16 values over NVLink and does
 
 from __future__ import annotations
 
-import math
 import os
 
 import torch
@@ -76,30 +76,33 @@ def eligible(params, grads, buffers, variances=None) -> bool:
             and len({p.dtype for p in params}) == 1 and len({g.dtype for g in grads}) == 1)
 
 
-class _AllReduce:
-    """Sum of a device tensor over the group through a double-buffered staging
-    region in symmetric memory (push, barrier, local fp32 slot sum)."""
+class _Region:
+    """The batch's Gram and norm buffers placed in symmetric memory, so the
+    partial Gram kernel writes straight into the memory the all-reduce reads.
 
-    def __init__(self, ws):
+    The all-reduce is in place: one bounded barrier (every partial written),
+    ``allreduce_inplace`` (rank r sums chunk r over all ranks and writes the sum
+    to every rank: NVLS ``multimem.ld_reduce`` / ``multimem.st`` when the buffer
+    has an NVSwitch multicast address, P2P loads and stores otherwise), and a
+    second barrier (every sum visible; nobody rewrites a chunk a peer still reads).
+    """
+
+    def __init__(self, ws, B: int, Cp: int):
         self.ws = ws
-        self.calls = 0
+        self.a_bytes = B * Cp * Cp * 2
+        self.s_bytes = 256
+        buf, self.peers = ws.buffer(self.a_bytes + self.s_bytes)
+        self.a = buf[: self.a_bytes].view(torch.bfloat16).view(B, Cp, Cp)
+        self.sums = buf[self.a_bytes : self.a_bytes + self.s_bytes].view(torch.float32)
 
-    def __call__(self, t: Tensor) -> None:
+    def allreduce(self, off: int, nbytes: int, dtype_code: int) -> None:
         ws = self.ws
-        flat = t.view(-1)
-        nbytes = flat.numel() * flat.element_size()
-        assert nbytes % 16 == 0 and flat.numel() % 8 == 0
-        half = ws.world * nbytes
-        buf, peers = ws.buffer(2 * half)
-        off = (self.calls % 2) * half
-        self.calls += 1
-        C = _ext.load()
-        C.push_slots(flat, peers, off, nbytes, ws.rank, ws.world, False, COMM_CTAS)
-        ws.barrier()  # every rank's partial has landed in every staging
-        C.local_slot_sum(flat, buf, off, ws.world, 1.0, 2 * COMM_CTAS)
+        ws.barrier()
+        _ext.load().allreduce_inplace(self.peers, off, nbytes, dtype_code, ws.rank, ws.world, ws.mc_base,
+                                      2 * COMM_CTAS)
+        ws.barrier()
 
 
-_REDUCERS: dict[int, _AllReduce] = {}
 
 
 def sharded_update(
@@ -126,12 +129,14 @@ def sharded_update(
     n_r = sl.r1 - sl.r0
     device = grads[0].to_local().device
     ws = symm.workspace_for(sl.group, device, "sharded_ns")
-    reduce_ = _REDUCERS.setdefault(id(ws), _AllReduce(ws))
     B = len(params)
+    if B > 64:
+        raise ValueError("sharded orthogonalisation takes at most 64 matrices per batch")
     Cp, Mp = round_up(C, 256), round_up(max(n_r, 1), 256)
+    region = _Region(ws, B, Cp)
     x = WORKSPACE.get(device, "shx", (B, Cp, Mp))
     x2 = WORKSPACE.get(device, "shx2", (B, Cp, Mp))
-    a_ws = WORKSPACE.get(device, "sha", (B, Cp, Cp))
+    a_ws = region.a
     b_ws = WORKSPACE.get(device, "shb", (B, Cp, Cp))
     loc = [(p.to_local(), g.to_local(), b.to_local()) for p, g, b in zip(params, grads, buffers, strict=True)]
     vec_ok = all(t.data_ptr() % 16 == 0 for trip in loc for t in trip)
@@ -149,17 +154,17 @@ def sharded_update(
     else:
         x.zero_()
         sumsq = torch.zeros(B, dtype=torch.float32, device=device)
-    sums = torch.zeros(8 * math.ceil(B / 8), dtype=torch.float32, device=device)
-    sums[:B] = sumsq
-    reduce_(sums)
-    inv = 1.0 / (sums[:B].sqrt() * norm_factor(strategy) + eps)
+    region.sums.zero_()
+    region.sums[:B] = sumsq
+    region.allreduce(region.a_bytes, region.s_bytes, 0)
+    inv = 1.0 / (region.sums[:B].sqrt() * norm_factor(strategy) + eps)
     c = coeffs.tolist()
     cur, nxt = x, x2
     for s in range(ns_steps):
         first = s == 0
         sc = inv if first else None
         C_.gram_sym2(cur, a_ws, None, sc, 1.0, 0.0, 2 if first else 0, 0)  # partial G = s^2 X_r^T X_r
-        reduce_(a_ws)
+        region.allreduce(0, region.a_bytes, 1)
         C_.gram_sym2(a_ws, b_ws, a_ws, None, c[s][2], c[s][1], 0, 0)  # B = c G^2 + b G
         C_.gemm_ax2(b_ws, cur, nxt, cur, sc, 1.0, c[s][0], 1 if first else 0, 1 if first else 0)
         cur, nxt = nxt, cur
@@ -177,3 +182,18 @@ def sharded_update(
             else mat_scale
         C_.muon_apply_ex(res, True, n_r, C, C, pp, pdt, None, ms, lr, float(weight_decay), bool(cautious_wd),
                          vec_ok)
+
+
+def sharded_reference(shards: list[Tensor], steps: int, strategy: str, eps: float = 1e-7) -> list[Tensor]:
+    """PyTorch statement of the sharded iteration (fp32, no communication): the
+    row blocks ``shards`` of one matrix in, their orthogonalised blocks out. Used
+    as the CPU oracle for the algorithm; equals the gathered iteration up to rounding."""
+    coeffs = coefficient_table(strategy, steps).tolist()
+    xs = [s.float() for s in shards]
+    norm = torch.sqrt(sum((x * x).sum() for x in xs))
+    xs = [x / (norm * norm_factor(strategy) + eps) for x in xs]
+    for a, b, c in coeffs:
+        G = sum(x.mT @ x for x in xs)  # the all-reduced partial Grams
+        Bm = b * G + c * (G @ G)
+        xs = [a * x + x @ Bm for x in xs]
+    return xs

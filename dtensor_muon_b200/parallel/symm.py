@@ -22,6 +22,14 @@ import torch.distributed as dist
 from ..ops import _ext
 
 
+def nvls_enabled() -> bool:
+    """Use NVSwitch multicast (``multimem``) where the symmetric allocation has a
+    multicast address; ``DMB_NVLS=0`` turns it off (the failure-detection tests
+    do, because a rank that dies while bound to a multicast object has raised
+    NVLink faults on its peers on this hardware)."""
+    return os.environ.get("DMB_NVLS", "1") != "0"
+
+
 def available() -> bool:
     if os.environ.get("DMB_DISABLE_SYMM", "0") == "1":
         return False
@@ -58,6 +66,8 @@ class SymmetricWorkspace:
         self.epoch = 0
         self._buf: torch.Tensor | None = None
         self.peer_base: torch.Tensor | None = None
+        # NVSwitch multicast address of the current buffer (0: none / disabled)
+        self.mc_base = 0
         self._keep = [hdl]
 
     def barrier(self) -> None:
@@ -78,6 +88,7 @@ class SymmetricWorkspace:
             buf = self._symm.empty(size, dtype=torch.uint8, device=self.device)
             hdl = self._symm.rendezvous(buf, self.group.group_name)
             self.peer_base = torch.tensor(list(hdl.buffer_ptrs), dtype=torch.int64).to(self.device)
+            self.mc_base = int(getattr(hdl, "multicast_ptr", 0) or 0) if nvls_enabled() else 0
             self._buf = buf
             self._keep.append(hdl)
         return self._buf, self.peer_base

@@ -233,3 +233,17 @@ def _foreach_sign_worker(rank, world):
 
 def test_dtensor_foreach_sign_strategy_gloo():
     run_distributed(_foreach_sign_worker, 2)
+
+
+@pytest.mark.parametrize("strategy", ["newton_schulz", "polar_express"])
+@pytest.mark.parametrize("splits", [(40, 24), (16, 16, 16, 16), (64, 0)])
+def test_sharded_iteration_equals_gathered(strategy, splits):
+    """Right-multiplied iteration on row shards with summed partial Grams equals
+    the gathered left-multiplied iteration (fp64 on the full matrix)."""
+    from dtensor_muon_b200.parallel.sharded_ns import sharded_reference
+
+    torch.manual_seed(9)
+    X = torch.randn(sum(splits), 24, dtype=torch.float64)
+    want = (ns_loop if strategy == "newton_schulz" else pe_loop)(X, 5, eps=1e-7)
+    got = torch.cat(sharded_reference(list(X.split(list(splits))), 5, strategy), dim=0)
+    torch.testing.assert_close(got.double(), want, rtol=1e-4, atol=1e-4)
