@@ -43,37 +43,53 @@ __device__ __forceinline__ float block_max(float v, float* red) {
   return red[0];
 }
 
-// Nearest entry of a dynamic-tree code map, ties to the lower index, in closed
-// form (no search). The map (dynamic_tree_map in optim_lp.py) is sorted: P
-// negative magnitudes, Z zeros, P positive magnitudes (unsigned: 1 zero, then
-// P). Decade k (0 <= k < V) holds n_k = 2^(V-k-1) magnitudes
-// (0.1 + 0.9 (i+1)/n_k) 10^-k, i < n_k, so the magnitudes <= t > 0 number
-//   (2^(V-k-1) - 1) + clamp(floor((t 10^k - 0.1) n_k / 0.9), 0, n_k),
-// where k is t's decade (t in (10^-(k+1), 10^-k]); this count is exact even
-// when k is off by one at a decade edge. From it, lo = (entries <= x) - 1; one
-// comparison each way against the map absorbs float rounding at exact code
-// values, then the nearer of lo, lo + 1 is taken as the binary search would.
+// Dynamic-tree code maps (dynamic_tree_map in optim_lp.py) in closed form: no
+// table lookups on the device. A map of n entries is sorted: P negative
+// magnitudes, Z zeros, P positive magnitudes (unsigned: 1 zero, then P).
+// Ascending magnitude j (0 <= j < P) lies in decade k = V - 1 - floor(log2(j+1)),
+// which holds n_k = 2^(V-k-1) values (0.1 + 0.9 (i+1)/n_k) 10^-k, i = j + 1 - n_k.
+// Every value is computed with the same correctly rounded float32 operations,
+// in the same order, as the host builds the table, so both agree bit for bit.
 struct TreeMap {
-  const float* q;   // the map, in shared memory
-  int n;            // entries (16 or 256)
-  int V;            // magnitude bits
-  int P;            // positive magnitudes (2^V - 1)
-  int neg0;         // index of the first entry >= 0 (P when signed, else 0)
+  int n;     // entries (16 or 256)
+  int V;     // magnitude bits
+  int P;     // positive magnitudes (2^V - 1)
+  int neg0;  // index of the first entry >= 0 (P when signed, else 0)
 
-  // A signed map starts at -1, an unsigned one at 0.
-  __device__ TreeMap(const float* smem_map, int entries) : q(smem_map), n(entries) {
+  __device__ TreeMap(int entries, bool sgn) : n(entries) {
     const int bits = entries == 256 ? 8 : 4;
-    const bool sgn = entries > 0 && smem_map[0] < 0.f;
     V = sgn ? bits - 1 : bits;
     P = (1 << V) - 1;
     neg0 = sgn ? P : 0;
   }
 };
 
+__device__ __forceinline__ float tree_mag(int V, int j) {
+  const int lg = 31 - __clz(j + 1);  // floor(log2(j + 1)) = V - 1 - k
+  const int nk = 1 << lg;
+  const int k = V - 1 - lg;
+  float p = 1.f;
+#pragma unroll
+  for (int q = 0; q < 7; ++q)
+    if (q < k) p = __fmul_rn(p, 0.1f);
+  const float f = __fadd_rn(0.1f, __fdiv_rn(__fmul_rn(0.9f, (float)(j + 2 - nk)), (float)nk));
+  return __fmul_rn(f, p);
+}
+
+// Value of sorted entry idx.
+__device__ __forceinline__ float tree_value(const TreeMap& m, int idx) {
+  if (idx < m.neg0) return -tree_mag(m.V, m.P - 1 - idx);
+  const int j = idx - (m.n - m.P);
+  return j < 0 ? 0.f : tree_mag(m.V, j);
+}
+
+// Magnitudes <= t (t >= 0), from t's decade k (t in (10^-(k+1), 10^-k]):
+//   (2^(V-k-1) - 1) + clamp(floor((t 10^k - 0.1) n_k / 0.9), 0, n_k).
+// Float rounding can move the count by one only when t is within rounding of
+// a code value, where either neighbour choice below still picks that code.
 __device__ __forceinline__ int tree_count_le(float t, int V) {
-  // magnitudes <= t, t >= 0
-  float pw = 1.f;   // 10^-k
-  float up = 1.f;   // 10^k
+  float pw = 1.f;  // 10^-k
+  float up = 1.f;  // 10^k
   int k = 0;
 #pragma unroll
   for (int j = 1; j < 8; ++j) {
@@ -90,33 +106,28 @@ __device__ __forceinline__ int tree_count_le(float t, int V) {
   return (nk - 1) + in_dec;
 }
 
+// Nearest entry, ties to the lower index (what a binary search over the sorted
+// table returns): lo = (entries <= x) - 1, then the nearer of lo and lo + 1.
 __device__ __forceinline__ int nearest_code(const TreeMap& m, float x) {
   int le;  // entries <= x
-  if (x >= 0.f) {
+  if (x >= 0.f)
     le = m.neg0 + (m.n - m.neg0 - m.P) + tree_count_le(x, m.V);
-  } else {
-    // negatives <= x: magnitudes >= |x| = P - (magnitudes < |x|); magnitudes < |x|
-    // equals those <= |x| except at an exact code value, fixed below
+  else  // negatives <= x: magnitudes >= |x|
     le = m.P - tree_count_le(-x, m.V);
-  }
-  int lo = min(max(le - 1, 0), m.n - 2);
-  if (lo + 1 <= m.n - 2 && m.q[lo + 1] <= x) ++lo;
-  if (lo + 1 <= m.n - 2 && m.q[lo + 1] <= x) ++lo;
-  if (lo > 0 && m.q[lo] > x) --lo;
-  if (lo > 0 && m.q[lo] > x) --lo;
+  const int lo = min(max(le - 1, 0), m.n - 2);
   const int hi = lo + 1;
-  return (fabsf(m.q[hi] - x) < fabsf(x - m.q[lo])) ? hi : lo;
+  return (fabsf(tree_value(m, hi) - x) < fabsf(x - tree_value(m, lo))) ? hi : lo;
 }
 
-__device__ __forceinline__ float decode(const uint8_t* codes, int fmt, long long i, const float* qmap) {
+__device__ __forceinline__ float decode(const uint8_t* codes, int fmt, long long i, const TreeMap& m) {
   if (fmt == 0) {
     __nv_fp8_e4m3 c;
     c.__x = codes[i];
     return float(c);
   }
-  if (fmt == 1) return qmap[codes[i]];
+  if (fmt == 1) return tree_value(m, codes[i]);
   const uint8_t byte = codes[i >> 1];
-  return qmap[(i & 1) ? (byte >> 4) : (byte & 15)];
+  return tree_value(m, (i & 1) ? (byte >> 4) : (byte & 15));
 }
 
 struct LpArgs {
@@ -145,11 +156,8 @@ __device__ __forceinline__ float lp_update(const LpArgs& a, float m, float g, lo
 // Generic path: one CTA per quantisation block, element e of the block on
 // thread e % LP_THREADS; any block size <= 4096 and any alignment.
 __global__ void __launch_bounds__(LP_THREADS) lp_step_kernel(const LpArgs a) {
-  __shared__ float qmap[256];
   __shared__ float red[LP_THREADS / 32];
-  for (int i = threadIdx.x; i < a.qn; i += LP_THREADS) qmap[i] = a.qmap_g[i];
-  __syncthreads();
-  const TreeMap tm(qmap, a.qn);
+  const TreeMap tm(a.qn, a.fmt != 0 && __ldg(a.qmap_g) < 0.f);
   const long long b0 = (long long)blockIdx.x * a.block;
   const int len = (int)min((long long)a.block, a.n - b0);
   constexpr int PER = 16;  // supports block <= LP_THREADS * PER = 4096
@@ -165,7 +173,7 @@ __global__ void __launch_bounds__(LP_THREADS) lp_step_kernel(const LpArgs a) {
       if (a.quant_in) {
         m = a.quant_in[i];
       } else {
-        m = decode(a.codes, a.fmt, i, qmap) * s_old;
+        m = decode(a.codes, a.fmt, i, tm) * s_old;
         if (a.has_grad) {
           const float g = a.grad_dtype == 0 ? reinterpret_cast<const float*>(a.grad)[i]
                                             : __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(a.grad)[i]);
@@ -223,7 +231,7 @@ constexpr int LP_VEC = 8;
 constexpr int LP_RUNS = 4096 / (LP_VEC * LP_THREADS);  // 2
 
 template <int FMT>
-__device__ __forceinline__ void decode8(const LpArgs& a, long long i, const float* qmap, float* v) {
+__device__ __forceinline__ void decode8(const LpArgs& a, long long i, const TreeMap& tm, float* v) {
   if constexpr (FMT == 0) {
     const uint2 w = *reinterpret_cast<const uint2*>(a.codes + i);
     const uint32_t ws[2] = {w.x, w.y};
@@ -237,11 +245,11 @@ __device__ __forceinline__ void decode8(const LpArgs& a, long long i, const floa
     const uint2 w = *reinterpret_cast<const uint2*>(a.codes + i);
     const uint32_t ws[2] = {w.x, w.y};
 #pragma unroll
-    for (int j = 0; j < 8; ++j) v[j] = qmap[(ws[j >> 2] >> (8 * (j & 3))) & 0xff];
+    for (int j = 0; j < 8; ++j) v[j] = tree_value(tm, (ws[j >> 2] >> (8 * (j & 3))) & 0xff);
   } else {
     const uint32_t w = *reinterpret_cast<const uint32_t*>(a.codes + (i >> 1));
 #pragma unroll
-    for (int j = 0; j < 8; ++j) v[j] = qmap[(w >> (4 * j)) & 15];
+    for (int j = 0; j < 8; ++j) v[j] = tree_value(tm, (w >> (4 * j)) & 15);
   }
 }
 
@@ -271,12 +279,8 @@ __device__ __forceinline__ void encode8(const LpArgs& a, long long i, const Tree
 
 template <int FMT>
 __global__ void __launch_bounds__(LP_THREADS) lp_step_vec_kernel(const LpArgs a) {
-  __shared__ float qmap[256];
   __shared__ float red[LP_THREADS / 32];
-  if (FMT != 0)
-    for (int i = threadIdx.x; i < a.qn; i += LP_THREADS) qmap[i] = a.qmap_g[i];
-  __syncthreads();
-  const TreeMap tm(qmap, a.qn);
+  const TreeMap tm(a.qn, FMT != 0 && __ldg(a.qmap_g) < 0.f);
   const long long b0 = (long long)blockIdx.x * a.block;
   const int len = (int)min((long long)a.block, a.n - b0);
   const float s_old = a.quant_in ? 0.f : a.scale[blockIdx.x];
@@ -293,7 +297,7 @@ __global__ void __launch_bounds__(LP_THREADS) lp_step_vec_kernel(const LpArgs a)
         v[r][0] = x0.x; v[r][1] = x0.y; v[r][2] = x0.z; v[r][3] = x0.w;
         v[r][4] = x1.x; v[r][5] = x1.y; v[r][6] = x1.z; v[r][7] = x1.w;
       } else {
-        decode8<FMT>(a, i, qmap, v[r]);
+        decode8<FMT>(a, i, tm, v[r]);
 #pragma unroll
         for (int j = 0; j < 8; ++j) v[r][j] *= s_old;
         if (a.has_grad) {

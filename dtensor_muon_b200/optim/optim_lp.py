@@ -38,6 +38,22 @@ FMT_FP8, FMT_8BIT, FMT_4BIT = 0, 1, 2
 _FMT_BITS = {FMT_8BIT: 8, FMT_4BIT: 4}
 
 
+def _tree_mag(V: int, j: int) -> float:
+    """Ascending magnitude ``j`` of a ``V``-bit dynamic-tree map, built with
+    correctly rounded float32 operations in a fixed order (the CUDA kernels
+    evaluate the same expression, so device and table agree bit for bit)."""
+    import numpy as np
+
+    f32 = np.float32
+    lg = (j + 1).bit_length() - 1
+    nk, k = 1 << lg, V - 1 - lg
+    p = f32(1.0)
+    for _ in range(k):
+        p = f32(p * f32(0.1))
+    f = f32(f32(0.1) + f32(f32(f32(0.9) * f32(j + 2 - nk)) / f32(nk)))
+    return float(f32(f * p))
+
+
 def dynamic_tree_map(total_bits: int, signed: bool = True) -> Tensor:
     """Sorted code map of dynamic tree quantisation (Dettmers, arXiv:1511.04561).
 
@@ -45,12 +61,10 @@ def dynamic_tree_map(total_bits: int, signed: bool = True) -> Tensor:
     ``10**-k`` and the bits after the first one-bit split ``(0.1, 1]`` of that
     decade into equal steps (right edges, so 1.0 itself is a code). Zero is a
     code; a signed map is padded with a second zero to ``2**total_bits`` entries.
+    Values are float32 results of one fixed expression (:func:`_tree_mag`).
     """
     value_bits = total_bits - (1 if signed else 0)
-    mags: list[float] = []
-    for k in range(value_bits):
-        n = 2 ** (value_bits - k - 1)
-        mags += [(0.1 + 0.9 * (i + 1) / n) * 10.0 ** (-k) for i in range(n)]
+    mags = [_tree_mag(value_bits, j) for j in range(2**value_bits - 1)]
     vals = [0.0] + mags + ([-m for m in mags] if signed else [])
     while len(vals) < 2**total_bits:
         vals.append(0.0)

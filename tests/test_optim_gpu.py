@@ -248,7 +248,7 @@ def test_native_adamw_edge_values_match_torch(n):
     and scalar paths: same results as torch.optim.AdamW, no NaN introduced."""
     g = torch.zeros(n)
     g[: n // 4] = 1e-20  # g^2 ~ 1e-40: subnormal fp32
-    g[n // 4 : n // 2] = torch.randn(n // 4, generator=torch.Generator().manual_seed(4))
+    g[n // 4 : n // 2] = torch.randn(n // 2 - n // 4, generator=torch.Generator().manual_seed(4))
     g[7] = 1e20  # g^2 overflows to inf
     a = nn.Parameter(torch.randn(n, generator=torch.Generator().manual_seed(5)).cuda())
     b = nn.Parameter(a.detach().clone())

@@ -100,8 +100,10 @@ def test_lp_state_dict_round_trip(tmp_path):
 
 def _closed_form_codes(x, qmap):
     """float32 restatement of the CUDA kernel's closed-form nearest code
-    (``nearest_code`` in ops/csrc/lp_quant.cu), vectorised with numpy."""
+    (``nearest_code`` / ``tree_value`` in ops/csrc/lp_quant.cu), vectorised with numpy."""
     import numpy as np
+
+    from dtensor_muon_b200.optim.optim_lp import _tree_mag
 
     q = qmap.numpy().astype(np.float32)
     n = q.size
@@ -111,6 +113,13 @@ def _closed_form_codes(x, qmap):
     P = (1 << V) - 1
     neg0 = P if sgn else 0
     x = x.numpy().astype(np.float32)
+    mags = np.array([_tree_mag(V, j) for j in range(P)], dtype=np.float32)
+
+    def value(idx):
+        j = idx - (n - P)
+        neg = -mags[np.clip(P - 1 - idx, 0, P - 1)]
+        pos = mags[np.clip(j, 0, P - 1)]
+        return np.where(idx < neg0, neg, np.where(j < 0, np.float32(0), pos))
 
     def count_le(t):
         pw = np.ones_like(t)
@@ -129,12 +138,18 @@ def _closed_form_codes(x, qmap):
 
     le = np.where(x >= 0, neg0 + (n - neg0 - P) + count_le(np.abs(x)), P - count_le(np.abs(x)))
     lo = np.clip(le - 1, 0, n - 2)
-    for _ in range(2):
-        lo = np.where((lo + 1 <= n - 2) & (q[np.minimum(lo + 1, n - 1)] <= x), lo + 1, lo)
-    for _ in range(2):
-        lo = np.where((lo > 0) & (q[lo] > x), lo - 1, lo)
     hi = lo + 1
-    return torch.from_numpy(np.where(np.abs(q[hi] - x) < np.abs(x - q[lo]), hi, lo).astype(np.uint8))
+    return torch.from_numpy(np.where(np.abs(value(hi) - x) < np.abs(x - value(lo)), hi, lo).astype(np.uint8))
+
+
+def test_closed_form_values_equal_the_table():
+    from dtensor_muon_b200.optim.optim_lp import _tree_mag
+
+    for bits, signed in ((8, True), (4, True), (8, False), (4, False)):
+        q = dynamic_tree_map(bits, signed)
+        V = bits - 1 if signed else bits
+        mags = torch.tensor([_tree_mag(V, j) for j in range(2**V - 1)], dtype=torch.float32)
+        assert torch.equal(q[-(2**V - 1):], mags)
 
 
 @pytest.mark.parametrize("bits,signed", [(8, True), (4, True), (8, False), (4, False)])
