@@ -43,80 +43,67 @@ __device__ __forceinline__ float block_max(float v, float* red) {
   return red[0];
 }
 
-// Dynamic-tree code maps (dynamic_tree_map in optim_lp.py) in closed form: no
-// table lookups on the device. A map of n entries is sorted: P negative
-// magnitudes, Z zeros, P positive magnitudes (unsigned: 1 zero, then P).
-// Ascending magnitude j (0 <= j < P) lies in decade k = V - 1 - floor(log2(j+1)),
-// which holds n_k = 2^(V-k-1) values (0.1 + 0.9 (i+1)/n_k) 10^-k, i = j + 1 - n_k.
-// Every value is computed with the same correctly rounded float32 operations,
-// in the same order, as the host builds the table, so both agree bit for bit.
+// Dynamic-tree code maps (dynamic_tree_map in optim_lp.py). A map of n
+// entries is sorted: P negative magnitudes, Z zeros, P positive magnitudes
+// (unsigned: 1 zero, then P). Decade k (0 <= k < V) holds n_k = 2^(V-k-1)
+// magnitudes (0.1 + 0.9 (i+1)/n_k) 10^-k, i < n_k. Encoding needs no search:
+// the magnitudes <= t (t >= 0) number
+//   (n_k - 1) + clamp(floor((t 10^k - 0.1) n_k / 0.9), 0, n_k)
+// for t's decade k (t in (10^-(k+1), 10^-k]), and lo = (entries <= x) - 1.
+// Float rounding can move that count by one only when t is within rounding of
+// a code value, and then either neighbour pair still yields that code. The
+// nearer of lo and lo + 1 is taken (ties to lo), as a binary search would.
+// Per CTA the map and three per-decade constants live in shared memory.
+struct TreeSmem {
+  float q[256];    // the map
+  float up[8];     // 10^k
+  float cnt[8];    // n_k / 0.9
+  float lim[8];    // 10^-(k+1): decade k is (lim[k], lim[k-1]]
+};
+
 struct TreeMap {
+  const TreeSmem* t;
   int n;     // entries (16 or 256)
   int V;     // magnitude bits
   int P;     // positive magnitudes (2^V - 1)
-  int neg0;  // index of the first entry >= 0 (P when signed, else 0)
+  int zoff;  // entries below the first positive magnitude
 
-  __device__ TreeMap(int entries, bool sgn) : n(entries) {
+  __device__ TreeMap(const TreeSmem* sm, int entries, bool sgn) : t(sm), n(entries) {
     const int bits = entries == 256 ? 8 : 4;
     V = sgn ? bits - 1 : bits;
     P = (1 << V) - 1;
-    neg0 = sgn ? P : 0;
+    zoff = entries - P;
   }
 };
 
-__device__ __forceinline__ float tree_mag(int V, int j) {
-  const int lg = 31 - __clz(j + 1);  // floor(log2(j + 1)) = V - 1 - k
-  const int nk = 1 << lg;
-  const int k = V - 1 - lg;
-  float p = 1.f;
-#pragma unroll
-  for (int q = 0; q < 7; ++q)
-    if (q < k) p = __fmul_rn(p, 0.1f);
-  const float f = __fadd_rn(0.1f, __fdiv_rn(__fmul_rn(0.9f, (float)(j + 2 - nk)), (float)nk));
-  return __fmul_rn(f, p);
+// Fill the shared tables (all threads of the CTA call this, then __syncthreads).
+__device__ __forceinline__ void tree_smem_fill(TreeSmem* sm, const float* qmap_g, int qn, int V) {
+  for (int i = threadIdx.x; i < qn; i += blockDim.x) sm->q[i] = qmap_g[i];
+  if (threadIdx.x < 8) {
+    const int k = threadIdx.x;
+    float up = 1.f, lim = 1.f;
+    for (int j = 0; j < k; ++j) up *= 10.f;
+    for (int j = 0; j <= k; ++j) lim *= 0.1f;
+    sm->up[k] = up;
+    sm->cnt[k] = k < V ? (float)(1 << (V - k - 1)) / 0.9f : 0.f;
+    sm->lim[k] = lim;
+  }
 }
 
-// Value of sorted entry idx.
-__device__ __forceinline__ float tree_value(const TreeMap& m, int idx) {
-  if (idx < m.neg0) return -tree_mag(m.V, m.P - 1 - idx);
-  const int j = idx - (m.n - m.P);
-  return j < 0 ? 0.f : tree_mag(m.V, j);
-}
-
-// Magnitudes <= t (t >= 0), from t's decade k (t in (10^-(k+1), 10^-k]):
-//   (2^(V-k-1) - 1) + clamp(floor((t 10^k - 0.1) n_k / 0.9), 0, n_k).
-// Float rounding can move the count by one only when t is within rounding of
-// a code value, where either neighbour choice below still picks that code.
-__device__ __forceinline__ int tree_count_le(float t, int V) {
-  float pw = 1.f;  // 10^-k
-  float up = 1.f;  // 10^k
+__device__ __forceinline__ int tree_count_le(const TreeMap& m, float t) {
   int k = 0;
 #pragma unroll
-  for (int j = 1; j < 8; ++j) {
-    if (j < V && t <= pw * 0.1f) {
-      pw *= 0.1f;
-      up *= 10.f;
-      k = j;
-    }
-  }
-  if (k == V - 1 && t < pw * 0.1f) return 0;  // below the smallest decade
-  const int nk = 1 << (V - k - 1);
-  const float f = floorf((t * up - 0.1f) * (float)nk / 0.9f);
-  const int in_dec = (int)fminf(fmaxf(f, 0.f), (float)nk);
-  return (nk - 1) + in_dec;
+  for (int j = 0; j < 7; ++j) k += (j < m.V - 1 && t <= m.t->lim[j]) ? 1 : 0;
+  // (below the smallest decade the floor is negative and the count is n_k - 1 = 0)
+  const int nk = 1 << (m.V - k - 1);
+  const float f = floorf(fmaf(t, m.t->up[k], -0.1f) * m.t->cnt[k]);
+  return (nk - 1) + (int)fminf(fmaxf(f, 0.f), (float)nk);
 }
 
-// Nearest entry, ties to the lower index (what a binary search over the sorted
-// table returns): lo = (entries <= x) - 1, then the nearer of lo and lo + 1.
 __device__ __forceinline__ int nearest_code(const TreeMap& m, float x) {
-  int le;  // entries <= x
-  if (x >= 0.f)
-    le = m.neg0 + (m.n - m.neg0 - m.P) + tree_count_le(x, m.V);
-  else  // negatives <= x: magnitudes >= |x|
-    le = m.P - tree_count_le(-x, m.V);
+  const int le = x >= 0.f ? m.zoff + tree_count_le(m, x) : m.P - tree_count_le(m, -x);
   const int lo = min(max(le - 1, 0), m.n - 2);
-  const int hi = lo + 1;
-  return (fabsf(tree_value(m, hi) - x) < fabsf(x - tree_value(m, lo))) ? hi : lo;
+  return (fabsf(m.t->q[lo + 1] - x) < fabsf(x - m.t->q[lo])) ? lo + 1 : lo;
 }
 
 __device__ __forceinline__ float decode(const uint8_t* codes, int fmt, long long i, const TreeMap& m) {
@@ -125,9 +112,9 @@ __device__ __forceinline__ float decode(const uint8_t* codes, int fmt, long long
     c.__x = codes[i];
     return float(c);
   }
-  if (fmt == 1) return tree_value(m, codes[i]);
+  if (fmt == 1) return m.t->q[codes[i]];
   const uint8_t byte = codes[i >> 1];
-  return tree_value(m, (i & 1) ? (byte >> 4) : (byte & 15));
+  return m.t->q[(i & 1) ? (byte >> 4) : (byte & 15)];
 }
 
 struct LpArgs {
@@ -157,7 +144,11 @@ __device__ __forceinline__ float lp_update(const LpArgs& a, float m, float g, lo
 // thread e % LP_THREADS; any block size <= 4096 and any alignment.
 __global__ void __launch_bounds__(LP_THREADS) lp_step_kernel(const LpArgs a) {
   __shared__ float red[LP_THREADS / 32];
-  const TreeMap tm(a.qn, a.fmt != 0 && __ldg(a.qmap_g) < 0.f);
+  __shared__ TreeSmem tsm;
+  const bool sgn = a.fmt != 0 && __ldg(a.qmap_g) < 0.f;
+  const TreeMap tm(&tsm, a.qn, sgn);
+  if (a.fmt != 0) tree_smem_fill(&tsm, a.qmap_g, a.qn, tm.V);
+  __syncthreads();
   const long long b0 = (long long)blockIdx.x * a.block;
   const int len = (int)min((long long)a.block, a.n - b0);
   constexpr int PER = 16;  // supports block <= LP_THREADS * PER = 4096
@@ -232,6 +223,7 @@ constexpr int LP_RUNS = 4096 / (LP_VEC * LP_THREADS);  // 2
 
 template <int FMT>
 __device__ __forceinline__ void decode8(const LpArgs& a, long long i, const TreeMap& tm, float* v) {
+  const float* qmap = tm.t->q;
   if constexpr (FMT == 0) {
     const uint2 w = *reinterpret_cast<const uint2*>(a.codes + i);
     const uint32_t ws[2] = {w.x, w.y};
@@ -245,11 +237,11 @@ __device__ __forceinline__ void decode8(const LpArgs& a, long long i, const Tree
     const uint2 w = *reinterpret_cast<const uint2*>(a.codes + i);
     const uint32_t ws[2] = {w.x, w.y};
 #pragma unroll
-    for (int j = 0; j < 8; ++j) v[j] = tree_value(tm, (ws[j >> 2] >> (8 * (j & 3))) & 0xff);
+    for (int j = 0; j < 8; ++j) v[j] = qmap[(ws[j >> 2] >> (8 * (j & 3))) & 0xff];
   } else {
     const uint32_t w = *reinterpret_cast<const uint32_t*>(a.codes + (i >> 1));
 #pragma unroll
-    for (int j = 0; j < 8; ++j) v[j] = tree_value(tm, (w >> (4 * j)) & 15);
+    for (int j = 0; j < 8; ++j) v[j] = qmap[(w >> (4 * j)) & 15];
   }
 }
 
@@ -280,7 +272,11 @@ __device__ __forceinline__ void encode8(const LpArgs& a, long long i, const Tree
 template <int FMT>
 __global__ void __launch_bounds__(LP_THREADS) lp_step_vec_kernel(const LpArgs a) {
   __shared__ float red[LP_THREADS / 32];
-  const TreeMap tm(a.qn, FMT != 0 && __ldg(a.qmap_g) < 0.f);
+  __shared__ TreeSmem tsm;
+  const bool sgn = FMT != 0 && __ldg(a.qmap_g) < 0.f;
+  const TreeMap tm(&tsm, a.qn, sgn);
+  if (FMT != 0) tree_smem_fill(&tsm, a.qmap_g, a.qn, tm.V);
+  __syncthreads();
   const long long b0 = (long long)blockIdx.x * a.block;
   const int len = (int)min((long long)a.block, a.n - b0);
   const float s_old = a.quant_in ? 0.f : a.scale[blockIdx.x];

@@ -267,6 +267,26 @@ class _Group:
     pdt: int
 
 
+_TABLES: dict[tuple, tuple[Tensor, Tensor]] = {}
+_TABLES_MAX = 512
+
+
+def _tables(ptrs: list[list[int]], S: int, Bo: int, device) -> tuple[Tensor, Tensor]:
+    """Device pointer / owner tables of a batch, cached by content: parameters,
+    momentum buffers and (usually) gradients keep their addresses from step to
+    step, so the steady state makes no host-to-device copy here."""
+    key = (str(device), Bo, tuple(x for row in ptrs for x in row))
+    hit = _TABLES.get(key)
+    if hit is None:
+        if len(_TABLES) >= _TABLES_MAX:
+            _TABLES.pop(next(iter(_TABLES)))
+        meta64 = torch.tensor(ptrs, dtype=torch.int64).pin_memory().to(device, non_blocking=True)
+        owner_slot = [[b // Bo for b in range(S)], [b % Bo for b in range(S)]]
+        meta32 = torch.tensor(owner_slot, dtype=torch.int32).pin_memory().to(device, non_blocking=True)
+        hit = _TABLES[key] = (meta64, meta32)
+    return hit
+
+
 class _Spec:
     """One owner-compute batch: pointer tables, symmetric-buffer layout, kernel arguments."""
 
@@ -290,9 +310,7 @@ class _Spec:
             [params[i].to_local().data_ptr() for i in sel],
             [variances[i].to_local().data_ptr() for i in sel] if g.has_var else [0] * S,
         ]
-        self.meta64 = torch.tensor(ptrs, dtype=torch.int64).pin_memory().to(g.device, non_blocking=True)
-        owner_slot = [[b // Bo for b in range(S)], [b % Bo for b in range(S)]]
-        self.meta32 = torch.tensor(owner_slot, dtype=torch.int32).pin_memory().to(g.device, non_blocking=True)
+        self.meta64, self.meta32 = _tables(ptrs, S, Bo, g.device)
         self.floats = [float(g.momentum), float(lr_eff), float(g.weight_decay)]
         self.vec_ok = int(all(x % 16 == 0 for row in ptrs[:3] for x in row))
 

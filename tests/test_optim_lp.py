@@ -100,10 +100,8 @@ def test_lp_state_dict_round_trip(tmp_path):
 
 def _closed_form_codes(x, qmap):
     """float32 restatement of the CUDA kernel's closed-form nearest code
-    (``nearest_code`` / ``tree_value`` in ops/csrc/lp_quant.cu), vectorised with numpy."""
+    (``nearest_code`` in ops/csrc/lp_quant.cu), vectorised with numpy."""
     import numpy as np
-
-    from dtensor_muon_b200.optim.optim_lp import _tree_mag
 
     q = qmap.numpy().astype(np.float32)
     n = q.size
@@ -113,33 +111,34 @@ def _closed_form_codes(x, qmap):
     P = (1 << V) - 1
     neg0 = P if sgn else 0
     x = x.numpy().astype(np.float32)
-    mags = np.array([_tree_mag(V, j) for j in range(P)], dtype=np.float32)
 
-    def value(idx):
-        j = idx - (n - P)
-        neg = -mags[np.clip(P - 1 - idx, 0, P - 1)]
-        pos = mags[np.clip(j, 0, P - 1)]
-        return np.where(idx < neg0, neg, np.where(j < 0, np.float32(0), pos))
+    f32 = np.float32
+    lim = [f32(1.0)]
+    for _ in range(8):
+        lim.append(f32(lim[-1] * f32(0.1)))
+    lim = np.array(lim[1:], dtype=np.float32)  # lim[k] = 10^-(k+1)
+    up = [f32(1.0)]
+    for _ in range(8):
+        up.append(f32(up[-1] * f32(10.0)))
+    up = np.array(up, dtype=np.float32)
+    cnt = np.array([f32(f32(1 << (V - k - 1)) / f32(0.9)) if k < V else 0 for k in range(8)], dtype=np.float32)
 
     def count_le(t):
-        pw = np.ones_like(t)
-        up = np.ones_like(t)
         k = np.zeros(t.shape, dtype=np.int64)
-        for j in range(1, 8):
-            if j < V:
-                m = t <= pw * np.float32(0.1)
-                pw = np.where(m, pw * np.float32(0.1), pw).astype(np.float32)
-                up = np.where(m, up * np.float32(10.0), up).astype(np.float32)
-                k = np.where(m, j, k)
+        for j in range(7):
+            if j < V - 1:
+                k += (t <= lim[j]).astype(np.int64)
         nk = (1 << (V - k - 1)).astype(np.float32)
-        f = np.floor(((t * up - np.float32(0.1)) * nk / np.float32(0.9)).astype(np.float32))
-        c = (nk - 1 + np.clip(f, 0, nk)).astype(np.int64)
-        return np.where((k == V - 1) & (t < pw * np.float32(0.1)), 0, c)
+        fm = (t.astype(np.float64) * up[k].astype(np.float64) - np.float64(f32(0.1))).astype(np.float32)
+        f = np.floor((fm * cnt[k]).astype(np.float32))
+        return (nk - 1 + np.clip(f, 0, nk)).astype(np.int64)
 
-    le = np.where(x >= 0, neg0 + (n - neg0 - P) + count_le(np.abs(x)), P - count_le(np.abs(x)))
+    P_ = P
+    zoff = n - P_
+    le = np.where(x >= 0, zoff + count_le(np.abs(x)), P - count_le(np.abs(x)))
     lo = np.clip(le - 1, 0, n - 2)
     hi = lo + 1
-    return torch.from_numpy(np.where(np.abs(value(hi) - x) < np.abs(x - value(lo)), hi, lo).astype(np.uint8))
+    return torch.from_numpy(np.where(np.abs(q[hi] - x) < np.abs(x - q[lo]), hi, lo).astype(np.uint8))
 
 
 def test_closed_form_values_equal_the_table():
