@@ -63,16 +63,23 @@ struct TreeSmem {
 
 struct TreeMap {
   const TreeSmem* t;
-  int n;     // entries (16 or 256)
-  int V;     // magnitude bits
-  int P;     // positive magnitudes (2^V - 1)
-  int zoff;  // entries below the first positive magnitude
+  int n;       // entries (16 or 256)
+  int V;       // magnitude bits
+  int P;       // positive magnitudes (2^V - 1)
+  int zoff;    // entries below the first positive magnitude
+  float lim[7];  // decade thresholds 10^-(j+1), kept in registers (the same chain of products as the table)
 
   __device__ TreeMap(const TreeSmem* sm, int entries, bool sgn) : t(sm), n(entries) {
     const int bits = entries == 256 ? 8 : 4;
     V = sgn ? bits - 1 : bits;
     P = (1 << V) - 1;
     zoff = entries - P;
+    float l = 1.f;
+#pragma unroll
+    for (int j = 0; j < 7; ++j) {
+      l *= 0.1f;
+      lim[j] = l;
+    }
   }
 };
 
@@ -93,7 +100,7 @@ __device__ __forceinline__ void tree_smem_fill(TreeSmem* sm, const float* qmap_g
 __device__ __forceinline__ int tree_count_le(const TreeMap& m, float t) {
   int k = 0;
 #pragma unroll
-  for (int j = 0; j < 7; ++j) k += (j < m.V - 1 && t <= m.t->lim[j]) ? 1 : 0;
+  for (int j = 0; j < 7; ++j) k += (j < m.V - 1 && t <= m.lim[j]) ? 1 : 0;
   // (below the smallest decade the floor is negative and the count is n_k - 1 = 0)
   const int nk = 1 << (m.V - k - 1);
   const float f = floorf(fmaf(t, m.t->up[k], -0.1f) * m.t->cnt[k]);
