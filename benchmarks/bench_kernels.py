@@ -20,7 +20,7 @@ import torch
 
 sys.path.insert(0, os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
 
-from benchmarks.harness import bench, markdown_table, ortho_flops, peaks  # noqa: E402
+from benchmarks.harness import bench, clocks, markdown_table, ortho_flops, peaks  # noqa: E402
 
 CONFIG2 = [(1, 4096, 4096), (1, 4096, 14336), (1, 14336, 4096), (64, 1024, 1024)]
 QUICK = [(1, 4096, 4096), (8, 1024, 1024)]
@@ -53,8 +53,10 @@ def run(shapes, with_reference: bool) -> str:
         for B, R, C in shapes:
             torch.manual_seed(0)
             x = torch.randn(B, R, C, device="cuda").bfloat16()
+            x = x / x.float().norm(dim=(-2, -1), keepdim=True).bfloat16()  # Frobenius-normalised (config 2)
             mats = list(x.unbind(0))
-            ours = bench(lambda: ortho.orthogonalize_native(mats, 5, strategy))
+            with clocks() as ck:
+                ours = bench(lambda: ortho.orthogonalize_native(mats, 5, strategy), reps=20)
             tl = bench(lambda: torch_loop(strategy)(x))
             ref = None
             if with_reference:
@@ -64,9 +66,12 @@ def run(shapes, with_reference: bool) -> str:
                     ref = f"unavailable: {type(exc).__name__}"
             fl = ortho_flops(B, R, C)
             frac = fl / (ours * 1e-3) / (pk["bf16_tflops"] * 1e12)
-            rows.append([strategy, f"{B}x{R}x{C}", ours, tl, ref if ref is not None else "-", frac])
+            ck = ck.result or {}
+            rows.append([strategy, f"{B}x{R}x{C}", ours, tl, ref if ref is not None else "-", frac,
+                         ck.get("sm_mhz"), ",".join(ck.get("reasons", [])) or "none"])
     t1 = markdown_table(
-        ["strategy", "shape", "ours ms", "torch bf16 loop ms", "reference triton ms", f"dense frac of {pk['source']} peak"],
+        ["strategy", "shape", "ours ms", "torch bf16 loop ms", "reference triton ms",
+         f"dense frac of {pk['source']} burst peak ({pk['bf16_tflops']} TF)", "median SM MHz (ours)", "throttle"],
         rows,
     )
     grows = []

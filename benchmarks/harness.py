@@ -60,6 +60,29 @@ def bench(fn, *, warmup: int = 3, reps: int = 10, flush_l2: bool = True) -> floa
     return statistics.median(times)
 
 
+class clocks:
+    """``with clocks() as c: ...`` samples the SM clock of GPU 0 during the block
+    (bench.py's nvidia-smi sampler); ``c.result`` = {sm_mhz (median under load),
+    sm_max_mhz, reasons, samples}."""
+
+    def __init__(self, gpu_index: int = 0):
+        import sys
+
+        sys.path.insert(0, ROOT)
+        from bench import ClockSampler
+
+        self.sampler = ClockSampler(gpu_index)
+        self.result: dict | None = None
+
+    def __enter__(self):
+        self.sampler.start()
+        return self
+
+    def __exit__(self, *exc):
+        self.result = self.sampler.stop()
+        return False
+
+
 def ortho_flops(batch: int, rows: int, cols: int, steps: int = 5) -> float:
     """Dense FLOPs of the iteration: steps * (4 N^2 M + 2 N^3), N = min dim."""
     n, m = min(rows, cols), max(rows, cols)

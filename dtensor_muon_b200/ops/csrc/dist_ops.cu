@@ -388,6 +388,40 @@ __global__ void dist_barrier_kernel(const int64_t* flag_base, int rank, int worl
   __threadfence_system();
 }
 
+// Split barrier for pipelined owner compute. flags: uint32 [slots][world] in
+// every rank's flag buffer. flag_signal: after this stream's previous work,
+// rank announces `epoch` in slot `slot` of every peer (flags[slot][rank] = epoch,
+// release at system scope). flag_wait: returns once flags[slot][k] >= epoch for
+// every k of this rank's own buffer (acquire); bounded like the barrier.
+__global__ void flag_signal_kernel(const int64_t* flag_base, int slot, int rank, int world, unsigned epoch) {
+  const int k = threadIdx.x;
+  __threadfence_system();
+  if (k < world) {
+    unsigned* peer = reinterpret_cast<unsigned*>(flag_base[k]) + (long long)slot * world + rank;
+    asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(peer), "r"(epoch) : "memory");
+  }
+}
+
+__global__ void flag_wait_kernel(const int64_t* flag_base, int slot, int rank, int world, unsigned epoch, int* err) {
+  const int k = threadIdx.x;
+  if (k < world) {
+    const unsigned* mine = reinterpret_cast<const unsigned*>(flag_base[rank]) + (long long)slot * world + k;
+    const unsigned long long t0 = global_timer_ns();
+    while (true) {
+      unsigned v;
+      asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(mine) : "memory");
+      if ((int)(v - epoch) >= 0) break;
+      if (global_timer_ns() - t0 > kWaitTimeoutNs) {
+        atomicExch(err, (int)kErrPeerTimeout);
+        break;
+      }
+      __nanosleep(64);
+    }
+  }
+  __syncthreads();
+  __threadfence_system();
+}
+
 }  // namespace
 
 namespace {
@@ -503,6 +537,23 @@ void dist_apply(const at::Tensor& meta_i64, const at::Tensor& meta_i32, const at
     const int tiles_r = (rows + T - 1) / T;
     dist_apply_rows_kernel<<<dim3(tiles_r * a.tiles_c, B), NT, 0, st>>>(a);
   }
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+void flag_signal(const at::Tensor& flag_base, int64_t slot, int64_t rank, int64_t world, int64_t epoch) {
+  const at::cuda::CUDAGuard guard(flag_base.device());
+  TORCH_CHECK(world <= 1024 && slot >= 0);
+  flag_signal_kernel<<<1, (int)((world + 31) / 32 * 32), 0, at::cuda::getCurrentCUDAStream()>>>(
+      flag_base.data_ptr<int64_t>(), (int)slot, (int)rank, (int)world, (unsigned)epoch);
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+void flag_wait(const at::Tensor& flag_base, int64_t slot, int64_t rank, int64_t world, int64_t epoch) {
+  const at::cuda::CUDAGuard guard(flag_base.device());
+  TORCH_CHECK(world <= 1024 && slot >= 0);
+  flag_wait_kernel<<<1, (int)((world + 31) / 32 * 32), 0, at::cuda::getCurrentCUDAStream()>>>(
+      flag_base.data_ptr<int64_t>(), (int)slot, (int)rank, (int)world, (unsigned)epoch,
+      device_error_word(flag_base.get_device()));
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 

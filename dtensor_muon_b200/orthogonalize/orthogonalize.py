@@ -10,7 +10,9 @@ Local work goes to the native tcgen05 engine for CUDA tensors
 loops otherwise. DTensor inputs keep the reference's distribution contract:
 
 * ``zeropower``: gather the full matrix, orthogonalise, hand back a DTensor
-  with the input's placements;
+  with the input's placements; on CUDA, row-sharded matrices (fewer than half
+  as many as ranks) instead run the sharded iteration of
+  :mod:`dtensor_muon_b200.parallel.sharded_ns` with no gather;
 * ``foreach_zeropower``: stack the batch, redistribute so that every rank owns
   whole matrices (Shard(0) of the stack), orthogonalise locally, redistribute
   back and unbind;
@@ -103,6 +105,10 @@ def zeropower(
         use_native = use_triton
     _validate_orthogonalization_args(strategy, steps)
     if isinstance(G, DTensor):
+        if use_native and _sharded_ok([G]):
+            from ..parallel.sharded_ns import sharded_zeropower
+
+            return sharded_zeropower([G], steps, strategy, eps)[0]
         full = G.full_tensor()
         U = orthogonalize_local(full, steps, eps, strategy, use_native)
         U = DTensor.from_local(U, device_mesh=G.device_mesh, placements=(Replicate(),) * G.device_mesh.ndim)
@@ -128,6 +134,11 @@ def foreach_zeropower(
     if isinstance(Gs[0], DTensor):
         Gs_d = cast(list[DTensor], Gs)
         meta = get_dtensor_metadata(Gs_d)
+        if use_native and _sharded_ok(Gs_d):
+            # few row-sharded matrices over many ranks: iterate on the shards
+            from ..parallel.sharded_ns import sharded_zeropower
+
+            return cast(list[Tensor], sharded_zeropower(Gs_d, steps, strategy, eps))
         mesh = meta["device_mesh"]
         if _needs_gather_path(meta["placements"]):
             # FSDP over TP-sharded weights (_StridedShard + Shard): gather each
@@ -149,6 +160,15 @@ def foreach_zeropower(
     X = torch.stack(list(Gs))
     U = orthogonalize_local(X, steps, eps, strategy, use_native)
     return list(U.unbind(0))
+
+
+def _sharded_ok(gs: list[DTensor]) -> bool:
+    """Row-sharded CUDA matrices that the sharded iteration (no gather) takes."""
+    if gs[0].device_mesh.device_type != "cuda":
+        return False
+    from ..parallel import sharded_ns
+
+    return sharded_ns.zeropower_eligible(gs)
 
 
 def _split_over_mesh(full: Tensor, mesh, fn) -> Tensor:

@@ -11,7 +11,8 @@ result back (P2P loads inside the apply kernel). Sequence per batch:
 
 Matrices are assigned in contiguous chunks (matrix b -> rank b // ceil(B/W)),
 like a Shard(0) of the stacked batch. Inside :class:`deferred` (the Muon step
-uses it) all batches of the step run phase by phase with three barriers in total.
+uses it) all batches of the step run as one pipeline (:func:`_run_phases`):
+one barrier, then per-batch arrival / completion signals.
 """
 
 from __future__ import annotations
@@ -359,6 +360,18 @@ class _Spec:
 
 
 def _run_phases(ws, specs: list) -> None:
+    """All batches of a step, pipelined with per-batch signals instead of
+    step-wide barriers: one barrier (every reader of the previous step's results
+    is done), then
+
+        pack_j ; signal(arrived_j)                     for every batch j
+        wait(arrived_j) ; owner work_j ; signal(done_j) for every batch j
+        wait(done_j) ; apply_j                          for every batch j
+
+    An owner starts batch j as soon as every rank's shards of batch j have
+    landed, and a rank applies batch j as soon as every owner finished it, so
+    skew between ranks is absorbed per batch rather than at whole-step barriers.
+    Slots 2j and 2j + 1 of the workspace's signal array are batch j's."""
     total, base = 0, []
     for sp in specs:
         base.append(total)
@@ -366,18 +379,23 @@ def _run_phases(ws, specs: list) -> None:
     buf, peer_base = ws.buffer(total)
     for sp, b in zip(specs, base):
         sp.place(b)
-    with nvtx("dmb.owner.pack"):
-        ws.barrier()  # every reader of the previous step's results is done
-        for sp in specs:
-            sp.pack(peer_base)
-        ws.barrier()  # all shards have landed in the owners' workspaces
-    with nvtx("dmb.owner.compute"):
-        for sp in specs:
-            sp.compute(buf)
-    with nvtx("dmb.owner.apply"):
-        ws.barrier()  # owners' results are ready
-        for sp in specs:
-            sp.apply(peer_base)
+    groups = [specs[i : i + ws.SIGNAL_SLOTS // 2] for i in range(0, len(specs), ws.SIGNAL_SLOTS // 2)]
+    for grp in groups:
+        ws.barrier()  # every reader of the previous results (and of these slots) is done
+        epoch = ws.next_signal_epoch()
+        with nvtx("dmb.owner.pack"):
+            for j, sp in enumerate(grp):
+                sp.pack(peer_base)
+                ws.signal(2 * j, epoch)
+        with nvtx("dmb.owner.compute"):
+            for j, sp in enumerate(grp):
+                ws.wait(2 * j, epoch)
+                sp.compute(buf)
+                ws.signal(2 * j + 1, epoch)
+        with nvtx("dmb.owner.apply"):
+            for j, sp in enumerate(grp):
+                ws.wait(2 * j + 1, epoch)
+                sp.apply(peer_base)
 
 
 def fsdp3d_local_eligible(params, grads, buffers) -> bool:

@@ -104,6 +104,26 @@ class _Region:
 
 
 
+def _iterate(C_, region, x, x2, b_ws, sumsq, B, coeffs, ns_steps, strategy, eps):
+    """The all-reduced normalisation and ``ns_steps`` sharded iterations on the
+    packed local rows ``x`` (X_r^T); returns the result buffer and 1/||X||."""
+    a_ws = region.a
+    region.sums.zero_()
+    region.sums[:B] = sumsq
+    region.allreduce(region.a_bytes, region.s_bytes, 0)
+    inv = 1.0 / (region.sums[:B].sqrt() * norm_factor(strategy) + eps)
+    c = coeffs.tolist()
+    cur, nxt = x, x2
+    for s in range(ns_steps):
+        first = s == 0
+        sc = inv if first else None
+        C_.gram_sym2(cur, a_ws, None, sc, 1.0, 0.0, 2 if first else 0, 0)  # partial G = s^2 X_r^T X_r
+        region.allreduce(0, region.a_bytes, 1)
+        C_.gram_sym2(a_ws, b_ws, a_ws, None, c[s][2], c[s][1], 0, 0)  # B = c G^2 + b G
+        C_.gemm_ax2(b_ws, cur, nxt, cur, sc, 1.0, c[s][0], 1 if first else 0, 1 if first else 0)
+        cur, nxt = nxt, cur
+    return cur, inv
+
 
 def sharded_update(
     params: list[DTensor],
@@ -154,20 +174,7 @@ def sharded_update(
     else:
         x.zero_()
         sumsq = torch.zeros(B, dtype=torch.float32, device=device)
-    region.sums.zero_()
-    region.sums[:B] = sumsq
-    region.allreduce(region.a_bytes, region.s_bytes, 0)
-    inv = 1.0 / (region.sums[:B].sqrt() * norm_factor(strategy) + eps)
-    c = coeffs.tolist()
-    cur, nxt = x, x2
-    for s in range(ns_steps):
-        first = s == 0
-        sc = inv if first else None
-        C_.gram_sym2(cur, a_ws, None, sc, 1.0, 0.0, 2 if first else 0, 0)  # partial G = s^2 X_r^T X_r
-        region.allreduce(0, region.a_bytes, 1)
-        C_.gram_sym2(a_ws, b_ws, a_ws, None, c[s][2], c[s][1], 0, 0)  # B = c G^2 + b G
-        C_.gemm_ax2(b_ws, cur, nxt, cur, sc, 1.0, c[s][0], 1 if first else 0, 1 if first else 0)
-        cur, nxt = nxt, cur
+    cur, inv = _iterate(C_, region, x, x2, b_ws, sumsq, B, coeffs, ns_steps, strategy, eps)
     if n_r == 0:
         return
     mat_scale = inv if ns_steps == 0 else None
@@ -182,6 +189,53 @@ def sharded_update(
             else mat_scale
         C_.muon_apply_ex(res, True, n_r, C, C, pp, pdt, None, ms, lr, float(weight_decay), bool(cautious_wd),
                          vec_ok)
+
+
+def zeropower_eligible(gs: list) -> bool:
+    """A batch of row-sharded 2-D CUDA DTensors the orthogonalisation-only
+    entry (:func:`sharded_zeropower`) takes: same rule as the optimizer path."""
+    if not gs or not all(isinstance(g, DTensor) for g in gs):
+        return False
+    return eligible(gs, gs, [], None) and all(g.to_local().dtype in (torch.float32, torch.bfloat16) for g in gs)
+
+
+def sharded_zeropower(gs: list[DTensor], steps: int, strategy: str, eps: float = 1e-7) -> list[DTensor]:
+    """Orthogonalise row-sharded matrices without gathering them; returns bf16
+    DTensors with the inputs' placements (each rank computes its own rows)."""
+    C_ = _ext.load()
+    coeffs = coefficient_table(strategy, steps)
+    sl = shard_layout(gs[0])
+    R, C = gs[0].shape
+    n_r = sl.r1 - sl.r0
+    device = gs[0].to_local().device
+    ws = symm.workspace_for(sl.group, device, "sharded_ns")
+    B = len(gs)
+    if B > 64:
+        raise ValueError("sharded orthogonalisation takes at most 64 matrices per batch")
+    Cp, Mp = round_up(C, 256), round_up(max(n_r, 1), 256)
+    region = _Region(ws, B, Cp)
+    x = WORKSPACE.get(device, "shx", (B, Cp, Mp))
+    x2 = WORKSPACE.get(device, "shx2", (B, Cp, Mp))
+    b_ws = WORKSPACE.get(device, "shb", (B, Cp, Cp))
+    loc = [g.to_local().contiguous() for g in gs]
+    if len({t.dtype for t in loc}) != 1:
+        loc = [t.float() for t in loc]
+    if n_r > 0:
+        ptrs = ptr_tensor([t.data_ptr() for t in loc], device)
+        vec_ok = all(t.data_ptr() % 16 == 0 for t in loc)
+        sumsq = C_.muon_pack_ex(ptrs, None, dtype_code(loc[0].dtype), n_r, C, C, True, x, 0.0, False, False,
+                                vec_ok).sum(dim=1)
+    else:
+        x.zero_()
+        sumsq = torch.zeros(B, dtype=torch.float32, device=device)
+    cur, inv = _iterate(C_, region, x, x2, b_ws, sumsq, B, coeffs, steps, strategy, eps)
+    if n_r > 0:
+        out = C_.muon_unpack(cur, True, n_r, C, inv if steps == 0 else None)
+    else:
+        out = torch.empty(B, 0, C, dtype=torch.bfloat16, device=device)
+    meta = dict(device_mesh=gs[0].device_mesh, placements=gs[0].placements, shape=gs[0].shape,
+                stride=gs[0].stride(), run_check=False)
+    return [DTensor.from_local(o, **meta) for o in out.unbind(0)]
 
 
 def sharded_reference(shards: list[Tensor], steps: int, strategy: str, eps: float = 1e-7) -> list[Tensor]:

@@ -75,6 +75,35 @@ class SymmetricWorkspace:
         self.epoch = (self.epoch + 1) & 0x7FFFFFFF
         _ext.load().dist_barrier(self.flag_ptrs, self.rank, self.world, self.epoch)
 
+    # -- split barrier: per-slot signals (pipelined owner compute) ----------------
+    SIGNAL_SLOTS = 256
+
+    def _signal_ptrs(self) -> torch.Tensor:
+        if getattr(self, "_sig_ptrs", None) is None:
+            flags = self._symm.empty(self.SIGNAL_SLOTS * self.world, dtype=torch.int32, device=self.device)
+            flags.zero_()
+            hdl = self._symm.rendezvous(flags, self.group.group_name)
+            self._sig_ptrs = torch.tensor(list(hdl.buffer_ptrs), dtype=torch.int64).to(self.device)
+            self._keep += [flags, hdl]
+            torch.cuda.synchronize(self.device)
+            dist.barrier(self.group)
+            self.sig_epoch = 0
+        return self._sig_ptrs
+
+    def next_signal_epoch(self) -> int:
+        """A fresh epoch for one round of signals (every rank calls this in step)."""
+        self._signal_ptrs()
+        self.sig_epoch = (self.sig_epoch + 1) & 0x7FFFFFFF
+        return self.sig_epoch
+
+    def signal(self, slot: int, epoch: int) -> None:
+        """After this stream's work so far: tell every rank that this rank reached ``slot``."""
+        _ext.load().flag_signal(self._signal_ptrs(), slot % self.SIGNAL_SLOTS, self.rank, self.world, epoch)
+
+    def wait(self, slot: int, epoch: int) -> None:
+        """Stream-ordered bounded wait until every rank has signalled ``slot`` in ``epoch``."""
+        _ext.load().flag_wait(self._signal_ptrs(), slot % self.SIGNAL_SLOTS, self.rank, self.world, epoch)
+
     def buffer(self, nbytes: int) -> tuple[torch.Tensor, torch.Tensor]:
         """Local view of at least ``nbytes`` symmetric bytes and the [world] tensor of peer base addresses.
 

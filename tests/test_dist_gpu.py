@@ -142,3 +142,35 @@ def test_sharded_newton_schulz_matches_single_process(strategy):
     (tall shapes), against the single-process step."""
     run_distributed(_sharded_worker, 2, args=(strategy, "float32"), backend="nccl", device_type="cuda",
                     timeout_s=120)
+
+
+def _zeropower_worker(rank, world):
+    import torch
+    from torch.distributed.device_mesh import init_device_mesh
+    from torch.distributed.tensor import Shard, distribute_tensor
+
+    from dtensor_muon_b200.ops import _ext, ortho
+    from dtensor_muon_b200.orthogonalize import foreach_zeropower, zeropower
+
+    device = torch.device("cuda", rank)
+    mesh = init_device_mesh("cuda", (world,))
+    gen = torch.Generator().manual_seed(4)
+    for shape in [(4096, 1024), (2048, 2048), (1000, 600)]:
+        full = torch.randn(shape, generator=gen).to(device)
+        d = distribute_tensor(full, mesh, [Shard(0)])
+        for strategy in ("newton_schulz", "polar_express"):
+            want = ortho.orthogonalize_native([full], 5, strategy)[0]
+            got = zeropower(d, steps=5, strategy=strategy)
+            assert list(got.placements) == [Shard(0)] and got.dtype == torch.bfloat16
+            assert_close(got.full_tensor(), want, rtol=2e-2, atol=2e-2, max_mismatch_pct=1.0, msg=f"{shape}")
+            (got2,) = foreach_zeropower([d], steps=5, strategy=strategy)
+            assert_close(got2.full_tensor(), want, rtol=2e-2, atol=2e-2, max_mismatch_pct=1.0)
+    torch.cuda.synchronize()
+    _ext.check_device_errors(device)
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+def test_sharded_zeropower_matches_gathered():
+    """Public zeropower / foreach_zeropower on a row-sharded matrix (no gather,
+    all-reduced partial Grams) against the single-GPU engine on the full matrix."""
+    run_distributed(_zeropower_worker, 2, backend="nccl", device_type="cuda", timeout_s=120)

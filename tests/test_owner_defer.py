@@ -65,3 +65,48 @@ def test_exception_drops_the_queue(calls):
             raise RuntimeError("step failed")
     assert calls == []
     assert "pending" not in oc._DEFER and not oc._DEFER.get("on")
+
+
+def test_pipeline_issue_order_uses_per_batch_signals():
+    """One barrier per step; batch j's owner work waits only for batch j's
+    arrivals, and its apply only for batch j's completion."""
+    log = []
+
+    class WS:
+        SIGNAL_SLOTS = 256
+
+        def buffer(self, n):
+            return "buf", "peers"
+
+        def barrier(self):
+            log.append("barrier")
+
+        def next_signal_epoch(self):
+            return 7
+
+        def signal(self, slot, epoch):
+            log.append(f"signal{slot}@{epoch}")
+
+        def wait(self, slot, epoch):
+            log.append(f"wait{slot}@{epoch}")
+
+    class Spec:
+        def __init__(self, n):
+            self.n, self.nbytes = n, 10
+
+        def place(self, b):
+            pass
+
+        def pack(self, peers):
+            log.append(f"pack{self.n}")
+
+        def compute(self, buf):
+            log.append(f"compute{self.n}")
+
+        def apply(self, peers):
+            log.append(f"apply{self.n}")
+
+    oc._run_phases(WS(), [Spec(0), Spec(1)])
+    assert log == ["barrier", "pack0", "signal0@7", "pack1", "signal2@7",
+                   "wait0@7", "compute0", "signal1@7", "wait2@7", "compute1", "signal3@7",
+                   "wait1@7", "apply0", "wait3@7", "apply1"]
