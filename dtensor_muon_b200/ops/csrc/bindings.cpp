@@ -67,6 +67,7 @@ void allreduce_inplace(const at::Tensor& peer_base, int64_t off, int64_t nbytes,
                        int64_t world, int64_t mc_base, int64_t max_ctas);
 void flag_signal(const at::Tensor& flag_base, int64_t slot, int64_t rank, int64_t world, int64_t epoch);
 void flag_wait(const at::Tensor& flag_base, int64_t slot, int64_t rank, int64_t world, int64_t epoch);
+void multimem_reduce_to_local(at::Tensor& out, int64_t mc_addr, double scale, int64_t max_ctas);
 void local_slot_sum(at::Tensor& out, const at::Tensor& staging_bytes, int64_t off, int64_t world, double scale,
                     int64_t max_ctas);
 void rs_sum_momentum(at::Tensor& out, const at::Tensor& staging_bytes, int64_t off, int64_t world, double scale,
@@ -143,6 +144,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("pull_slots", &dmb::pull_slots);
   m.def("allreduce_inplace", &dmb::allreduce_inplace);
   m.def("flag_signal", &dmb::flag_signal);
+  m.def("multimem_reduce_to_local", &dmb::multimem_reduce_to_local);
   m.def("flag_wait", &dmb::flag_wait);
   m.def("rs_sum_momentum", &dmb::rs_sum_momentum);
   m.def("ep_scatter_rows", &dmb::ep_scatter_rows);

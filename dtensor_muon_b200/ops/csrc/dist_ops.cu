@@ -690,6 +690,36 @@ __global__ void allreduce_inplace_kernel(const int64_t* peer_base, long long off
   }
 }
 
+// out[i] = scale * (sum over ranks of their value at multicast address mc + 16 i
+// bytes): one multimem.ld_reduce per 16 bytes (the NVSwitch reduces), then a
+// plain store into this GPU's `out`. The reduce-scatter of FSDP gradients over
+// NVLS: every rank's full input sits at the same offset of its symmetric
+// staging, and rank r reduces only its own chunk.
+__global__ void multimem_reduce_to_local_kernel(uint4* __restrict__ out, long long mc, long long nvec, int dt,
+                                                float scale) {
+  const long long stride = (long long)gridDim.x * blockDim.x;
+  for (long long v = (long long)blockIdx.x * blockDim.x + threadIdx.x; v < nvec; v += stride) {
+    uint32_t r[4];
+    const void* addr = reinterpret_cast<const void*>(mc + v * 16);
+    if (dt == 0) {
+      mm_ld_reduce_f32x4(addr, r);
+      if (scale != 1.f)
+#pragma unroll
+        for (int e = 0; e < 4; ++e) r[e] = __float_as_uint(__uint_as_float(r[e]) * scale);
+    } else {
+      mm_ld_reduce_bf16x8(addr, r);
+      if (scale != 1.f)
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const float lo = bf16_bits_to_float((uint16_t)(r[e] & 0xFFFFu)) * scale;
+          const float hi = bf16_bits_to_float((uint16_t)(r[e] >> 16)) * scale;
+          r[e] = pack_bf16x2(lo, hi);
+        }
+    }
+    out[v] = make_uint4(r[0], r[1], r[2], r[3]);
+  }
+}
+
 // out[i] = scale * sum_j staging[j * n + i] (local), dt 0 fp32 / 1 bf16.
 __global__ void local_slot_sum_kernel(void* __restrict__ out, const void* __restrict__ staging, long long n, int world,
                                       int dt, float scale) {
@@ -749,6 +779,20 @@ void allreduce_inplace(const at::Tensor& peer_base, int64_t off, int64_t nbytes,
   const int blocks = (int)std::max<long long>(1, std::min<long long>(max_ctas, (per + 255) / 256));
   allreduce_inplace_kernel<<<blocks, 256, 0, at::cuda::getCurrentCUDAStream()>>>(
       peer_base.data_ptr<int64_t>(), off, nvec, (int)dtype_code, (int)rank, (int)world, mc_base);
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+void multimem_reduce_to_local(at::Tensor& out, int64_t mc_addr, double scale, int64_t max_ctas) {
+  const at::cuda::CUDAGuard guard(out.device());
+  TORCH_CHECK(out.is_contiguous() && (out.scalar_type() == at::kFloat || out.scalar_type() == at::kBFloat16));
+  const long long nbytes = out.numel() * out.element_size();
+  TORCH_CHECK(nbytes % 16 == 0 && mc_addr % 16 == 0 && mc_addr != 0 &&
+              reinterpret_cast<uintptr_t>(out.data_ptr()) % 16 == 0);
+  const long long nvec = nbytes / 16;
+  if (nvec == 0) return;
+  const int blocks = (int)std::max<long long>(1, std::min<long long>(max_ctas, (nvec + 255) / 256));
+  multimem_reduce_to_local_kernel<<<blocks, 256, 0, at::cuda::getCurrentCUDAStream()>>>(
+      reinterpret_cast<uint4*>(out.data_ptr()), mc_addr, nvec, out.scalar_type() == at::kFloat ? 0 : 1, (float)scale);
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 

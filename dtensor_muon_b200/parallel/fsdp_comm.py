@@ -70,12 +70,22 @@ def _staging(purpose: str) -> _PushStaging:
     return _STAGING[purpose]
 
 
-# All-gather scheme: "pull" (default) copies this rank's shard into its own
-# staging slot, passes one barrier and pulls every slot straight into FSDP's
-# output (P2P loads); "push" stores the shard into every peer's staging, passes
-# the barrier and copies the W slots into the output locally (one extra
-# full-size local copy).
-AG_MODE = os.environ.get("DMB_AG_MODE", "pull")
+# All-gather scheme. Every scheme puts this rank's shard into its own staging
+# slot (or every peer's), passes one bounded barrier and then fills FSDP's output:
+#  "ce" (default): W - 1 device copies from the peers' slots straight into the
+#       output, executed by the copy engines: no SM is taken from the model
+#       GEMMs that overlap the all-gather;
+#  "pull": the same transfer by the pull_slots kernel (P2P loads on SMs);
+#  "push": push_slots stores the shard into every peer's staging, then one
+#       local copy of the W slots into the output.
+AG_MODE = os.environ.get("DMB_AG_MODE", "ce")
+# Reduce-scatter scheme: "auto" (default) = "nvls" where the staging has an
+# NVSwitch multicast address, else "ce"; "nvls": this rank's full input goes
+# into its own staging by a copy-engine copy, barrier, then one
+# multimem.ld_reduce kernel reads the sum of its own chunk through the switch;
+# "ce": the W chunks go to the owners' staging by copy-engine copies, barrier,
+# local fp32 slot sum; "push": the same with the push_slots kernel.
+RS_MODE = os.environ.get("DMB_RS_MODE", "auto")
 
 
 class P2PAllGather(AllGather):
@@ -94,11 +104,20 @@ class P2PAllGather(AllGather):
         world = dist.get_world_size(group)
         ws, buf, peers, off = self._stage.half(group, output_tensor.device, nbytes * world)
         C = _ext.load()
-        if AG_MODE == "pull":
+        if AG_MODE in ("ce", "pull"):
             mine = off + ws.rank * nbytes
-            buf[mine : mine + nbytes].copy_(input_tensor.view(-1).view(torch.uint8))
+            src = input_tensor.view(-1).view(torch.uint8)
+            buf[mine : mine + nbytes].copy_(src)
             ws.barrier()  # every rank's shard is in its own staging slot
-            C.pull_slots(output_tensor.view(-1), peers, off, nbytes, ws.rank, world, COMM_CTAS)
+            if AG_MODE == "pull":
+                C.pull_slots(output_tensor.view(-1), peers, off, nbytes, ws.rank, world, COMM_CTAS)
+                return None
+            out = output_tensor.view(-1).view(torch.uint8)
+            if src.data_ptr() != out.data_ptr() + ws.rank * nbytes:  # FSDP's input is normally this slot
+                out[ws.rank * nbytes : (ws.rank + 1) * nbytes].copy_(src)
+            for j in range(1, world):
+                k = (ws.rank + j) % world
+                out[k * nbytes : (k + 1) * nbytes].copy_(ws.peer_bytes(k, off + k * nbytes, nbytes))
             return None
         C.push_slots(input_tensor, peers, off, nbytes, ws.rank, world, False, COMM_CTAS)
         ws.barrier()  # every shard has landed in every rank's staging
@@ -138,9 +157,29 @@ class P2PReduceScatter(ReduceScatter):
         slot = output_tensor.numel() * output_tensor.element_size()
         ws, buf, peers, off = self._stage.half(group, output_tensor.device, slot * world)
         C = _ext.load()
-        C.push_slots(input_tensor, peers, off, slot, ws.rank, world, True, COMM_CTAS)
-        ws.barrier()  # every rank's chunk for me has landed
         segs = self._fused.segments(self._module, output_tensor, world) if self._fused is not None else None
+        mode = RS_MODE
+        if mode == "auto":
+            mode = "nvls" if ws.mc_base else "ce"
+        if mode == "nvls" and ws.mc_base and segs is None:
+            # my full input at my staging offset; the switch sums chunk `rank` over all ranks
+            buf[off : off + slot * world].copy_(input_tensor.view(-1).view(torch.uint8))
+            ws.barrier()  # every rank's input is in its staging
+            C.multimem_reduce_to_local(output_tensor, ws.mc_base + off + ws.rank * slot, scale, COMM_CTAS)
+            return None
+        if mode == "ce":
+            src = input_tensor.view(-1).view(torch.uint8)
+            for j in range(world):
+                k = (ws.rank + j) % world
+                dst = off + ws.rank * slot  # slot `rank` of peer k's staging
+                piece = src[k * slot : (k + 1) * slot]
+                if k == ws.rank:
+                    buf[dst : dst + slot].copy_(piece)
+                else:
+                    ws.peer_bytes(k, dst, slot).copy_(piece)
+        else:
+            C.push_slots(input_tensor, peers, off, slot, ws.rank, world, True, COMM_CTAS)
+        ws.barrier()  # every rank's chunk for me has landed
         if segs is not None:
             C.rs_sum_momentum(output_tensor, buf, off, world, scale, segs, 2 * COMM_CTAS)
         else:

@@ -118,9 +118,16 @@ class SymmetricWorkspace:
             hdl = self._symm.rendezvous(buf, self.group.group_name)
             self.peer_base = torch.tensor(list(hdl.buffer_ptrs), dtype=torch.int64).to(self.device)
             self.mc_base = int(getattr(hdl, "multicast_ptr", 0) or 0) if nvls_enabled() else 0
+            self._hdl = hdl
             self._buf = buf
             self._keep.append(hdl)
         return self._buf, self.peer_base
+
+    def peer_bytes(self, k: int, off: int, nbytes: int) -> torch.Tensor:
+        """uint8 view of rank ``k``'s symmetric buffer at ``off`` (a tensor on this
+        device whose memory is the peer's; copies from or to it go over NVLink,
+        by the copy engines when issued as a plain device copy)."""
+        return self._hdl.get_buffer(k, (nbytes,), torch.uint8, off)
 
     def check(self) -> None:
         _ext.check_device_errors(self.device)

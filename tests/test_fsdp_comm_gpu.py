@@ -9,7 +9,7 @@ from testkit import run_distributed
 pytestmark = [pytest.mark.gpu, pytest.mark.multigpu]
 
 
-def _worker(rank, world, ag_mode="pull"):
+def _worker(rank, world, ag_mode="ce", rs_mode="auto"):
     import torch
     from torch.distributed.device_mesh import init_device_mesh
 
@@ -19,6 +19,7 @@ def _worker(rank, world, ag_mode="pull"):
     from dtensor_muon_b200.train import build_llama, build_optimizer
 
     fsdp_comm.AG_MODE = ag_mode
+    fsdp_comm.RS_MODE = rs_mode
 
     mesh = init_device_mesh("cuda", (world,))
     cfg = preset("tiny", vocab_size=1024, dim=256, n_layers=2)
@@ -51,6 +52,8 @@ def _worker(rank, world, ag_mode="pull"):
 
 
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
-@pytest.mark.parametrize("ag_mode", ["pull", "push"])
-def test_fsdp_p2p_collectives_match_nccl(ag_mode):
-    run_distributed(_worker, 2, args=(ag_mode,), backend="nccl", device_type="cuda")
+@pytest.mark.parametrize("ag_mode,rs_mode", [("ce", "auto"), ("ce", "ce"), ("pull", "push"), ("push", "nvls")])
+def test_fsdp_p2p_collectives_match_nccl(ag_mode, rs_mode):
+    """Every all-gather / reduce-scatter scheme (copy engines, P2P kernels, NVLS
+    multimem reduce where the fabric has multicast) against FSDP2 on NCCL."""
+    run_distributed(_worker, 2, args=(ag_mode, rs_mode), backend="nccl", device_type="cuda")
