@@ -113,6 +113,48 @@ __device__ __forceinline__ int nearest_code(const TreeMap& m, float x) {
   return (fabsf(m.t->q[lo + 1] - x) < fabsf(x - m.t->q[lo])) ? lo + 1 : lo;
 }
 
+// Faster encoding for the persistent vector kernel: a per-CTA table indexed by
+// the top bits of |x| (8 exponent + LUT_MBITS mantissa bits, |x| >= 2^-24; below
+// that every magnitude is larger). lut[key] = magnitudes <= the bucket's lower
+// edge. A bucket is narrower (relative width 2^-8) than the closest pair of
+// magnitudes of any supported map (ratio >= 1.007), so at most one magnitude
+// lies inside it and one comparison completes the count.
+constexpr int LUT_MBITS = 8;
+constexpr int LUT_EMIN = 127 - 24;  // biased exponent of the first bucket
+constexpr int LUT_N = 25 << LUT_MBITS;
+
+__device__ __forceinline__ int lut_key(float t) {
+  const int k = (int)(__float_as_uint(t) >> (23 - LUT_MBITS)) - (LUT_EMIN << LUT_MBITS);
+  return min(max(k, 0), LUT_N - 1);
+}
+
+// Fill lut[] from the map in shared memory (binary search over the P ascending
+// magnitudes q[zoff .. n)); all threads call it, then __syncthreads.
+__device__ __forceinline__ void lut_fill(uint8_t* lut, const TreeMap& m) {
+  const float* mag = m.t->q + m.zoff;
+  for (int i = threadIdx.x; i < LUT_N; i += blockDim.x) {
+    const float edge = i == 0 ? 0.f : __uint_as_float((uint32_t)(i + (LUT_EMIN << LUT_MBITS)) << (23 - LUT_MBITS));
+    int lo = 0, hi = m.P;  // count of mag <= edge in [lo, hi]
+    while (lo < hi) {
+      const int mid = (lo + hi) >> 1;
+      if (mag[mid] <= edge)
+        lo = mid + 1;
+      else
+        hi = mid;
+    }
+    lut[i] = (uint8_t)lo;
+  }
+}
+
+__device__ __forceinline__ int nearest_code_lut(const TreeMap& m, const uint8_t* lut, float x) {
+  const float t = fabsf(x);
+  const int c = lut[lut_key(t)];
+  const int cnt = c + ((c < m.P && m.t->q[m.zoff + c] <= t) ? 1 : 0);  // magnitudes <= t
+  const int le = x >= 0.f ? m.zoff + cnt : m.P - cnt;
+  const int lo = min(max(le - 1, 0), m.n - 2);
+  return (fabsf(m.t->q[lo + 1] - x) < fabsf(x - m.t->q[lo])) ? lo + 1 : lo;
+}
+
 __device__ __forceinline__ float decode(const uint8_t* codes, int fmt, long long i, const TreeMap& m) {
   if (fmt == 0) {
     __nv_fp8_e4m3 c;
@@ -253,11 +295,12 @@ __device__ __forceinline__ void decode8(const LpArgs& a, long long i, const Tree
 }
 
 template <int FMT>
-__device__ __forceinline__ void encode8(const LpArgs& a, long long i, const TreeMap& tm, const float* v, float inv) {
+__device__ __forceinline__ void encode8(const LpArgs& a, long long i, const TreeMap& tm, const uint8_t* lut,
+                                        const float* v, float inv) {
   if constexpr (FMT == 2) {
     uint32_t w = 0;
 #pragma unroll
-    for (int j = 0; j < 8; ++j) w |= (uint32_t)nearest_code(tm, v[j] * inv) << (4 * j);
+    for (int j = 0; j < 8; ++j) w |= (uint32_t)nearest_code_lut(tm, lut, v[j] * inv) << (4 * j);
     *reinterpret_cast<uint32_t*>(a.codes + (i >> 1)) = w;
   } else {
     uint32_t ws[2] = {0u, 0u};
@@ -268,7 +311,7 @@ __device__ __forceinline__ void encode8(const LpArgs& a, long long i, const Tree
         __nv_fp8_e4m3 q(v[j] * inv);
         c = q.__x;
       } else {
-        c = (uint32_t)nearest_code(tm, v[j] * inv);
+        c = (uint32_t)nearest_code_lut(tm, lut, v[j] * inv);
       }
       ws[j >> 2] |= c << (8 * (j & 3));
     }
@@ -280,79 +323,88 @@ template <int FMT>
 __global__ void __launch_bounds__(LP_THREADS) lp_step_vec_kernel(const LpArgs a) {
   __shared__ float red[LP_THREADS / 32];
   __shared__ TreeSmem tsm;
+  __shared__ uint8_t lut[FMT != 0 ? LUT_N : 1];
   const bool sgn = FMT != 0 && __ldg(a.qmap_g) < 0.f;
   const TreeMap tm(&tsm, a.qn, sgn);
   if (FMT != 0) tree_smem_fill(&tsm, a.qmap_g, a.qn, tm.V);
   __syncthreads();
-  const long long b0 = (long long)blockIdx.x * a.block;
-  const int len = (int)min((long long)a.block, a.n - b0);
-  const float s_old = a.quant_in ? 0.f : a.scale[blockIdx.x];
-  float v[LP_RUNS][LP_VEC];
-  float amax = 0.f;
-#pragma unroll
-  for (int r = 0; r < LP_RUNS; ++r) {
-    const int e = (r * LP_THREADS + threadIdx.x) * LP_VEC;
-    if (e < len) {
-      const long long i = b0 + e;
-      if (a.quant_in) {
-        const float4 x0 = *reinterpret_cast<const float4*>(a.quant_in + i);
-        const float4 x1 = *reinterpret_cast<const float4*>(a.quant_in + i + 4);
-        v[r][0] = x0.x; v[r][1] = x0.y; v[r][2] = x0.z; v[r][3] = x0.w;
-        v[r][4] = x1.x; v[r][5] = x1.y; v[r][6] = x1.z; v[r][7] = x1.w;
-      } else {
-        decode8<FMT>(a, i, tm, v[r]);
-#pragma unroll
-        for (int j = 0; j < 8; ++j) v[r][j] *= s_old;
-        if (a.has_grad) {
-          float g[8];
-          if (a.grad_dtype == 0) {
-            const float4 g0 = *reinterpret_cast<const float4*>(reinterpret_cast<const float*>(a.grad) + i);
-            const float4 g1 = *reinterpret_cast<const float4*>(reinterpret_cast<const float*>(a.grad) + i + 4);
-            g[0] = g0.x; g[1] = g0.y; g[2] = g0.z; g[3] = g0.w;
-            g[4] = g1.x; g[5] = g1.y; g[6] = g1.z; g[7] = g1.w;
-          } else {
-            const uint4 w = *reinterpret_cast<const uint4*>(reinterpret_cast<const __nv_bfloat16*>(a.grad) + i);
-            const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&w);
-#pragma unroll
-            for (int j = 0; j < 4; ++j) {
-              const float2 f = __bfloat1622float2(h[j]);
-              g[2 * j] = f.x;
-              g[2 * j + 1] = f.y;
-            }
-          }
-          uint4 out;
-          __nv_bfloat162* o = reinterpret_cast<__nv_bfloat162*>(&out);
-#pragma unroll
-          for (int j = 0; j < 8; ++j) {
-            const float gj = a.maximize ? -g[j] : g[j];
-            v[r][j] = fmaf(v[r][j], a.momentum, gj);
-            g[j] = a.nesterov ? fmaf(v[r][j], a.momentum, gj) : v[r][j];
-          }
-#pragma unroll
-          for (int j = 0; j < 4; ++j) o[j] = __floats2bfloat162_rn(g[2 * j], g[2 * j + 1]);
-          if (a.gout) *reinterpret_cast<uint4*>(a.gout + i) = out;
-        }
-      }
-      if (a.dequant_out) {
-        *reinterpret_cast<float4*>(a.dequant_out + i) = make_float4(v[r][0], v[r][1], v[r][2], v[r][3]);
-        *reinterpret_cast<float4*>(a.dequant_out + i + 4) = make_float4(v[r][4], v[r][5], v[r][6], v[r][7]);
-      }
-    } else {
-#pragma unroll
-      for (int j = 0; j < 8; ++j) v[r][j] = 0.f;
-    }
-#pragma unroll
-    for (int j = 0; j < 8; ++j) amax = fmaxf(amax, fabsf(v[r][j]));
+  if (FMT != 0 && (a.has_grad || a.quant_in)) {
+    lut_fill(lut, tm);
+    __syncthreads();
   }
-  if (!a.has_grad && !a.quant_in) return;  // dequantise-only
-  amax = block_max(amax, red);
-  const float s_new = FMT == 0 ? amax / 448.f : amax;
-  const float inv = s_new > 0.f ? 1.f / s_new : 0.f;
-  if (threadIdx.x == 0) a.scale[blockIdx.x] = s_new;
+  const long long nblocks = (a.n + a.block - 1) / a.block;
+  // persistent: the table is built once per CTA and reused for every block
+  for (long long blk = blockIdx.x; blk < nblocks; blk += gridDim.x) {
+    const long long b0 = blk * a.block;
+    const int len = (int)min((long long)a.block, a.n - b0);
+    const float s_old = a.quant_in ? 0.f : a.scale[blk];
+    float v[LP_RUNS][LP_VEC];
+    float amax = 0.f;
 #pragma unroll
-  for (int r = 0; r < LP_RUNS; ++r) {
-    const int e = (r * LP_THREADS + threadIdx.x) * LP_VEC;
-    if (e < len) encode8<FMT>(a, b0 + e, tm, v[r], inv);
+    for (int r = 0; r < LP_RUNS; ++r) {
+      const int e = (r * LP_THREADS + threadIdx.x) * LP_VEC;
+      if (e < len) {
+        const long long i = b0 + e;
+        if (a.quant_in) {
+          const float4 x0 = *reinterpret_cast<const float4*>(a.quant_in + i);
+          const float4 x1 = *reinterpret_cast<const float4*>(a.quant_in + i + 4);
+          v[r][0] = x0.x; v[r][1] = x0.y; v[r][2] = x0.z; v[r][3] = x0.w;
+          v[r][4] = x1.x; v[r][5] = x1.y; v[r][6] = x1.z; v[r][7] = x1.w;
+        } else {
+          decode8<FMT>(a, i, tm, v[r]);
+#pragma unroll
+          for (int j = 0; j < 8; ++j) v[r][j] *= s_old;
+          if (a.has_grad) {
+            float g[8];
+            if (a.grad_dtype == 0) {
+              const float4 g0 = *reinterpret_cast<const float4*>(reinterpret_cast<const float*>(a.grad) + i);
+              const float4 g1 = *reinterpret_cast<const float4*>(reinterpret_cast<const float*>(a.grad) + i + 4);
+              g[0] = g0.x; g[1] = g0.y; g[2] = g0.z; g[3] = g0.w;
+              g[4] = g1.x; g[5] = g1.y; g[6] = g1.z; g[7] = g1.w;
+            } else {
+              const uint4 w = *reinterpret_cast<const uint4*>(reinterpret_cast<const __nv_bfloat16*>(a.grad) + i);
+              const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&w);
+#pragma unroll
+              for (int j = 0; j < 4; ++j) {
+                const float2 f = __bfloat1622float2(h[j]);
+                g[2 * j] = f.x;
+                g[2 * j + 1] = f.y;
+              }
+            }
+            uint4 out;
+            __nv_bfloat162* o = reinterpret_cast<__nv_bfloat162*>(&out);
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+              const float gj = a.maximize ? -g[j] : g[j];
+              v[r][j] = fmaf(v[r][j], a.momentum, gj);
+              g[j] = a.nesterov ? fmaf(v[r][j], a.momentum, gj) : v[r][j];
+            }
+#pragma unroll
+            for (int j = 0; j < 4; ++j) o[j] = __floats2bfloat162_rn(g[2 * j], g[2 * j + 1]);
+            if (a.gout) *reinterpret_cast<uint4*>(a.gout + i) = out;
+          }
+        }
+        if (a.dequant_out) {
+          *reinterpret_cast<float4*>(a.dequant_out + i) = make_float4(v[r][0], v[r][1], v[r][2], v[r][3]);
+          *reinterpret_cast<float4*>(a.dequant_out + i + 4) = make_float4(v[r][4], v[r][5], v[r][6], v[r][7]);
+        }
+      } else {
+#pragma unroll
+        for (int j = 0; j < 8; ++j) v[r][j] = 0.f;
+      }
+#pragma unroll
+      for (int j = 0; j < 8; ++j) amax = fmaxf(amax, fabsf(v[r][j]));
+    }
+    if (!a.has_grad && !a.quant_in) continue;  // dequantise-only
+    amax = block_max(amax, red);
+    const float s_new = FMT == 0 ? amax / 448.f : amax;
+    const float inv = s_new > 0.f ? 1.f / s_new : 0.f;
+    if (threadIdx.x == 0) a.scale[blk] = s_new;
+#pragma unroll
+    for (int r = 0; r < LP_RUNS; ++r) {
+      const int e = (r * LP_THREADS + threadIdx.x) * LP_VEC;
+      if (e < len) encode8<FMT>(a, b0 + e, tm, lut, v[r], inv);
+    }
   }
 }
 
@@ -377,12 +429,17 @@ void launch_lp(LpArgs a) {
   if (nblocks == 0) return;
   auto stream = at::cuda::getCurrentCUDAStream();
   if (lp_vec_ok(a)) {
+    // persistent grid: a few CTAs per SM, each looping over blocks
+    int dev = 0, sms = 148;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    const unsigned grid = (unsigned)std::min<long long>(nblocks, (long long)sms * 6);
     if (a.fmt == 0)
-      lp_step_vec_kernel<0><<<(unsigned)nblocks, LP_THREADS, 0, stream>>>(a);
+      lp_step_vec_kernel<0><<<grid, LP_THREADS, 0, stream>>>(a);
     else if (a.fmt == 1)
-      lp_step_vec_kernel<1><<<(unsigned)nblocks, LP_THREADS, 0, stream>>>(a);
+      lp_step_vec_kernel<1><<<grid, LP_THREADS, 0, stream>>>(a);
     else
-      lp_step_vec_kernel<2><<<(unsigned)nblocks, LP_THREADS, 0, stream>>>(a);
+      lp_step_vec_kernel<2><<<grid, LP_THREADS, 0, stream>>>(a);
   } else {
     lp_step_kernel<<<(unsigned)nblocks, LP_THREADS, 0, stream>>>(a);
   }

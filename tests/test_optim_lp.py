@@ -227,3 +227,49 @@ def test_quantized_dtensor_state_dcp_round_trip_gloo(tmp_path, cls_name):
     from dtensor_muon_b200.testing.distributed import run_distributed
 
     run_distributed(_lp_dcp_worker, 2, args=(str(tmp_path / "ckpt"), cls_name))
+
+
+def _lut_codes(x, qmap):
+    """numpy restatement of the persistent kernel's table-driven nearest code
+    (``lut_fill`` / ``nearest_code_lut`` in ops/csrc/lp_quant.cu)."""
+    import numpy as np
+
+    q = qmap.numpy().astype(np.float32)
+    n = q.size
+    bits = 8 if n == 256 else 4
+    V = bits - 1 if q[0] < 0 else bits
+    P = (1 << V) - 1
+    zoff = n - P
+    mag = q[zoff:]
+    MB, EMIN = 8, 127 - 24
+    N = 25 << MB
+    idx = np.arange(N, dtype=np.uint64)
+    edges = ((idx + (EMIN << MB)) << (23 - MB)).astype(np.uint32).view(np.float32)
+    edges[0] = 0.0
+    lut = np.searchsorted(mag, edges, side="right")  # magnitudes <= edge
+    x = x.numpy().astype(np.float32)
+    t = np.abs(x)
+    key = np.clip((t.view(np.uint32) >> (23 - MB)).astype(np.int64) - (EMIN << MB), 0, N - 1)
+    c = lut[key]
+    cnt = c + ((c < P) & (mag[np.minimum(c, P - 1)] <= t))
+    le = np.where(x >= 0, zoff + cnt, P - cnt)
+    lo = np.clip(le - 1, 0, n - 2)
+    hi = lo + 1
+    return torch.from_numpy(np.where(np.abs(q[hi] - x) < np.abs(x - q[lo]), hi, lo).astype(np.uint8))
+
+
+@pytest.mark.parametrize("bits,signed", [(8, True), (4, True), (8, False), (4, False)])
+def test_table_code_index_matches_search(bits, signed):
+    from dtensor_muon_b200.optim.optim_lp import _nearest_codes
+
+    qmap = dynamic_tree_map(bits, signed)
+    mids = (qmap[1:] + qmap[:-1]) / 2
+    base = torch.cat([qmap, mids, torch.rand(200000) * 2 - 1 if signed else torch.rand(200000),
+                      torch.tensor([1e-30, 3e-8, 1e-7, 1.0, 1.0000001])])
+    xs = torch.cat([base, torch.nextafter(base, torch.tensor(2.0)), torch.nextafter(base, torch.tensor(-2.0))])
+    if not signed:
+        xs = xs.clamp(min=0.0)
+    want = _nearest_codes(xs, qmap)
+    got = _lut_codes(xs, qmap)
+    bad = (want != got).nonzero().flatten()
+    assert bad.numel() == 0, [(xs[i].item(), want[i].item(), got[i].item()) for i in bad[:5]]
