@@ -77,9 +77,9 @@ def main():
         from install_reference import ensure_reference
 
         sys.path.insert(0, ensure_reference())
-        import torch._dynamo
+        import torch._dynamo as _dynamo
 
-        torch._dynamo.config.suppress_errors = True
+        _dynamo.config.suppress_errors = True
         from muonium.orthogonalize import foreach_zeropower_3d_fsdp, zeropower
 
         kw = {"use_triton": True}

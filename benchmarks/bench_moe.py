@@ -113,9 +113,9 @@ def run_reference(cfg, mesh, args, world, rank):
         from install_reference import ensure_reference
 
         sys.path.insert(0, ensure_reference())
-        import torch._dynamo
+        import torch._dynamo as _dynamo
 
-        torch._dynamo.config.suppress_errors = True  # reference pins torch 2.12; see bench.py
+        _dynamo.config.suppress_errors = True  # reference pins torch 2.12; see bench.py
         from muonium import MuonLP
         from transformers import MixtralConfig, MixtralForCausalLM
 

@@ -116,9 +116,9 @@ def build_reference(cfg, mesh, args):
     from install_reference import ensure_reference
 
     sys.path.insert(0, ensure_reference())
-    import torch._dynamo
+    import torch._dynamo as _dynamo
 
-    torch._dynamo.config.suppress_errors = True  # reference pins torch 2.12; see bench.py
+    _dynamo.config.suppress_errors = True  # reference pins torch 2.12; see bench.py
     from muonium import Muon as RefMuon
 
     hf_cfg = LlamaConfig(vocab_size=cfg.vocab_size, hidden_size=cfg.dim, intermediate_size=cfg.ffn_dim,
