@@ -116,7 +116,20 @@ def run_reference(cfg, mesh, args, world, rank):
         import torch._dynamo as _dynamo
 
         _dynamo.config.suppress_errors = True  # reference pins torch 2.12; see bench.py
-        from muonium import MuonLP
+        try:
+            from muonium import MuonLP
+
+            opt_name = "muonium.MuonLP (fp32 state, foreach=False)"
+        except ImportError:
+            # The reference's MuonLP module imports torchao at load time (not installable
+            # here). Its base class adds nothing to Muon but foreach=False and fp32 buffers,
+            # which muonium.Muon(foreach=False) is.
+            from muonium import Muon as _RefMuon
+
+            def MuonLP(groups, **kw):  # noqa: N802
+                return _RefMuon(groups, foreach=False, **kw)
+
+            opt_name = "muonium.Muon(foreach=False): the base MuonLP's math (MuonLP needs torchao)"
         from transformers import MixtralConfig, MixtralForCausalLM
 
         hf = MixtralConfig(vocab_size=cfg.vocab_size, hidden_size=cfg.dim, intermediate_size=cfg.ffn_dim,
@@ -179,7 +192,7 @@ def run_reference(cfg, mesh, args, world, rank):
         ms, opt_ms = st.tolist()
         print(json.dumps({"metric": "MoE train tokens/s", "impl": "reference", "value": world * args.seq / (ms / 1e3),
                           "ms_per_step": ms, "optimizer_step_ms": opt_ms, "n_gpus": world, "layers": args.layers,
-                          "opt": "muonium.MuonLP (fp32 state, foreach=False)", "parallelism": f"fsdp{world}",
+                          "opt": opt_name, "parallelism": f"fsdp{world}",
                           "dtype": "bf16", "data": "synthetic"}))
     dist.destroy_process_group()
 

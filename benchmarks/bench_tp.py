@@ -84,9 +84,16 @@ def main():
         opt.zero_grad(set_to_none=True)
         return o0, o1
 
-    for _ in range(args.warmup):
-        step()
-    torch.cuda.synchronize()
+    try:
+        for _ in range(args.warmup):
+            step()
+        torch.cuda.synchronize()
+    except Exception as exc:  # the reference's own step failed on this config: report it
+        if args.impl != "reference":
+            raise
+        if rank == 0:
+            print(json.dumps({"impl": "reference", "unavailable": f"{type(exc).__name__}: {exc}"[:400]}), flush=True)
+        os._exit(0)  # peers may be inside a collective
     dist.barrier()
     t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     t0.record()

@@ -652,18 +652,35 @@ __global__ void allreduce_inplace_kernel(const int64_t* peer_base, long long off
   const long long per = (nvec + world - 1) / world;
   const long long v0 = (long long)rank * per, v1 = min(nvec, v0 + per);
   const long long stride = (long long)gridDim.x * blockDim.x;
-  for (long long v = v0 + (long long)blockIdx.x * blockDim.x + threadIdx.x; v < v1; v += stride) {
-    const long long byte = off + v * 16;
-    uint32_t r[4];
-    if (mc_base != 0) {
-      void* mc = reinterpret_cast<void*>(mc_base + byte);
+  long long v = v0 + (long long)blockIdx.x * blockDim.x + threadIdx.x;
+  if (mc_base != 0) {
+    // NVLS: four independent switch reductions in flight per thread, then the broadcasts
+    for (; v + 3 * stride < v1; v += 4 * stride) {
+      uint32_t r[4][4];
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const void* mc = reinterpret_cast<const void*>(mc_base + off + (v + u * stride) * 16);
+        if (dt == 0)
+          mm_ld_reduce_f32x4(mc, r[u]);
+        else
+          mm_ld_reduce_bf16x8(mc, r[u]);
+      }
+#pragma unroll
+      for (int u = 0; u < 4; ++u) mm_st_16(reinterpret_cast<void*>(mc_base + off + (v + u * stride) * 16), r[u], dt);
+    }
+    for (; v < v1; v += stride) {
+      uint32_t r[4];
+      void* mc = reinterpret_cast<void*>(mc_base + off + v * 16);
       if (dt == 0)
         mm_ld_reduce_f32x4(mc, r);
       else
         mm_ld_reduce_bf16x8(mc, r);
       mm_st_16(mc, r, dt);
-      continue;
     }
+    return;
+  }
+  for (; v < v1; v += stride) {
+    const long long byte = off + v * 16;
     float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
     for (int j = 0; j < world; ++j) {
       const int k = (j + rank) % world;
@@ -690,32 +707,52 @@ __global__ void allreduce_inplace_kernel(const int64_t* peer_base, long long off
   }
 }
 
-// out[i] = scale * (sum over ranks of their value at multicast address mc + 16 i
-// bytes): one multimem.ld_reduce per 16 bytes (the NVSwitch reduces), then a
-// plain store into this GPU's `out`. The reduce-scatter of FSDP gradients over
-// NVLS: every rank's full input sits at the same offset of its symmetric
-// staging, and rank r reduces only its own chunk.
+__device__ __forceinline__ void mm_scale(uint32_t (&r)[4], int dt, float scale) {
+  if (scale == 1.f) return;
+  if (dt == 0) {
+#pragma unroll
+    for (int e = 0; e < 4; ++e) r[e] = __float_as_uint(__uint_as_float(r[e]) * scale);
+  } else {
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const float lo = bf16_bits_to_float((uint16_t)(r[e] & 0xFFFFu)) * scale;
+      const float hi = bf16_bits_to_float((uint16_t)(r[e] >> 16)) * scale;
+      r[e] = pack_bf16x2(lo, hi);
+    }
+  }
+}
+
+// Four independent multimem.ld_reduce per thread are issued before any result
+// is used: a switch reduction has microseconds of latency, so one in flight per
+// thread would leave the NVLink idle.
 __global__ void multimem_reduce_to_local_kernel(uint4* __restrict__ out, long long mc, long long nvec, int dt,
                                                 float scale) {
   const long long stride = (long long)gridDim.x * blockDim.x;
-  for (long long v = (long long)blockIdx.x * blockDim.x + threadIdx.x; v < nvec; v += stride) {
+  long long v = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+  for (; v + 3 * stride < nvec; v += 4 * stride) {
+    uint32_t r[4][4];
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      const void* addr = reinterpret_cast<const void*>(mc + (v + u * stride) * 16);
+      if (dt == 0)
+        mm_ld_reduce_f32x4(addr, r[u]);
+      else
+        mm_ld_reduce_bf16x8(addr, r[u]);
+    }
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      mm_scale(r[u], dt, scale);
+      out[v + u * stride] = make_uint4(r[u][0], r[u][1], r[u][2], r[u][3]);
+    }
+  }
+  for (; v < nvec; v += stride) {
     uint32_t r[4];
     const void* addr = reinterpret_cast<const void*>(mc + v * 16);
-    if (dt == 0) {
+    if (dt == 0)
       mm_ld_reduce_f32x4(addr, r);
-      if (scale != 1.f)
-#pragma unroll
-        for (int e = 0; e < 4; ++e) r[e] = __float_as_uint(__uint_as_float(r[e]) * scale);
-    } else {
+    else
       mm_ld_reduce_bf16x8(addr, r);
-      if (scale != 1.f)
-#pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          const float lo = bf16_bits_to_float((uint16_t)(r[e] & 0xFFFFu)) * scale;
-          const float hi = bf16_bits_to_float((uint16_t)(r[e] >> 16)) * scale;
-          r[e] = pack_bf16x2(lo, hi);
-        }
-    }
+    mm_scale(r, dt, scale);
     out[v] = make_uint4(r[0], r[1], r[2], r[3]);
   }
 }

@@ -74,18 +74,24 @@ def _staging(purpose: str) -> _PushStaging:
 # slot (or every peer's), passes one bounded barrier and then fills FSDP's output:
 #  "ce" (default): W - 1 device copies from the peers' slots straight into the
 #       output, executed by the copy engines: no SM is taken from the model
-#       GEMMs that overlap the all-gather;
+#       GEMMs that overlap the all-gather (W = 2, 436 MB: 0.49 ms alone vs
+#       NCCL 0.67 ms; under a concurrent GEMM loop 1.13 ms and +0.09 ms on the
+#       GEMMs, vs NCCL 1.59 ms and +0.50 ms);
 #  "pull": the same transfer by the pull_slots kernel (P2P loads on SMs);
 #  "push": push_slots stores the shard into every peer's staging, then one
 #       local copy of the W slots into the output.
 AG_MODE = os.environ.get("DMB_AG_MODE", "ce")
-# Reduce-scatter scheme: "auto" (default) = "nvls" where the staging has an
-# NVSwitch multicast address, else "ce"; "nvls": this rank's full input goes
-# into its own staging by a copy-engine copy, barrier, then one
-# multimem.ld_reduce kernel reads the sum of its own chunk through the switch;
-# "ce": the W chunks go to the owners' staging by copy-engine copies, barrier,
-# local fp32 slot sum; "push": the same with the push_slots kernel.
-RS_MODE = os.environ.get("DMB_RS_MODE", "auto")
+# Reduce-scatter scheme: "ce" (default): the W chunks go to their owners'
+# staging by copy-engine copies, barrier, local fp32 slot sum; "push": the same
+# with the push_slots kernel; "nvls": this rank's full input goes into its own
+# staging by a copy-engine copy, barrier, then one multimem.ld_reduce kernel
+# reads the sum of its own chunk through the switch (needs a multicast
+# address); "auto" = "ce". Measured at W = 2 on a 436 MB layer
+# (benchmarks/bench_fsdp_comm.py): ce 0.90 ms alone and 2.17 ms under a
+# concurrent GEMM loop that it slows by 0.22 ms; NCCL 0.72 / 2.39 ms, +1.06 ms;
+# push 0.83 / 2.46, +0.68; nvls 2.24 / 2.68, +0.36 (the full-size local copy
+# into staging dominates it).
+RS_MODE = os.environ.get("DMB_RS_MODE", "ce")
 
 
 class P2PAllGather(AllGather):
@@ -160,7 +166,7 @@ class P2PReduceScatter(ReduceScatter):
         segs = self._fused.segments(self._module, output_tensor, world) if self._fused is not None else None
         mode = RS_MODE
         if mode == "auto":
-            mode = "nvls" if ws.mc_base else "ce"
+            mode = "ce"
         if mode == "nvls" and ws.mc_base and segs is None:
             # my full input at my staging offset; the switch sums chunk `rank` over all ranks
             buf[off : off + slot * world].copy_(input_tensor.view(-1).view(torch.uint8))
