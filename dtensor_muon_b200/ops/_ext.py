@@ -36,6 +36,7 @@ _LAUNCHES = {
     "push_slots": 1,
     "local_slot_sum": 1,
     "rs_sum_momentum": 1,
+    "ag_gemm": 1,
     "ep_scatter_rows": 1,
     "ep_gather_rows": 1,
     "rope": 1,

@@ -63,6 +63,9 @@ void push_slots(const at::Tensor& src, const at::Tensor& peer_base, int64_t off,
                 int64_t world, bool per_peer, int64_t max_ctas);
 void pull_slots(at::Tensor& out, const at::Tensor& peer_base, int64_t off, int64_t slot_bytes, int64_t rank,
                 int64_t world, int64_t max_ctas);
+void ag_gemm(const at::Tensor& x, const at::Tensor& shard, at::Tensor& wg, at::Tensor& out,
+             const at::Tensor& peer_base, int64_t slot_off, const at::Tensor& flag_base, at::Tensor& counters,
+             int64_t rank, int64_t world, int64_t epoch, int64_t max_pairs);
 void allreduce_inplace(const at::Tensor& peer_base, int64_t off, int64_t nbytes, int64_t dtype_code, int64_t rank,
                        int64_t world, int64_t mc_base, int64_t max_ctas);
 void flag_signal(const at::Tensor& flag_base, int64_t slot, int64_t rank, int64_t world, int64_t epoch);
@@ -143,6 +146,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("local_slot_sum", &dmb::local_slot_sum);
   m.def("pull_slots", &dmb::pull_slots);
   m.def("allreduce_inplace", &dmb::allreduce_inplace);
+  m.def("ag_gemm", &dmb::ag_gemm);
   m.def("flag_signal", &dmb::flag_signal);
   m.def("multimem_reduce_to_local", &dmb::multimem_reduce_to_local);
   m.def("flag_wait", &dmb::flag_wait);
