@@ -143,7 +143,8 @@ def build_ours(args, world, device):
         from torch.distributed.device_mesh import init_device_mesh
 
         mesh = init_device_mesh("cuda", (world,))
-    model = build_llama(cfg, device, mesh=mesh, seed=0, fsdp_comm=args.fsdp_comm)
+    model = build_llama(cfg, device, mesh=mesh, seed=0, fsdp_comm=args.fsdp_comm,
+                        fused_gather=world > 1 and bool(args.fused_gather))
     opt = build_optimizer(model, Muon, lr=args.lr, wd=0.1, orthogonalization_strategy=args.strategy,
                           fuse_momentum=world > 1 and args.fsdp_comm == "p2p" and args.fuse_momentum)
     from dtensor_muon_b200.models.llama import lm_loss
@@ -254,6 +255,8 @@ def parse_args():
                     help="ours, N > 1: Muon momentum update inside the FSDP gradient reduce-scatter")
     ap.add_argument("--fsdp-comm", default=os.environ.get("DMB_FSDP_COMM", "p2p"), choices=["p2p", "nccl"],
                     help="ours: FSDP collectives on NVLink P2P kernels or NCCL")
+    ap.add_argument("--fused-gather", type=int, default=int(os.environ.get("DMB_FUSED_GATHER", "0")),
+                    help="ours, N > 1: q/k/v and gate/up weights gathered inside their forward GEMM")
     ap.add_argument("--ref-batch-size", type=int, default=32,
                     help="reference arm: Muon foreach batch_size (keeps its Gram kernel below 2**31 elements)")
     args = ap.parse_args()

@@ -85,12 +85,18 @@ class Attention(nn.Module):
         self.wk = nn.Linear(cfg.dim, cfg.n_kv_heads * cfg.head_dim, bias=False)
         self.wv = nn.Linear(cfg.dim, cfg.n_kv_heads * cfg.head_dim, bias=False)
         self.wo = nn.Linear(cfg.n_heads * cfg.head_dim, cfg.dim, bias=False)
+        # set by train.build_llama(fused_gather=True): q/k/v through the fused
+        # parameter all-gather + GEMM kernel (parallel.ag_gemm.GatherLinear)
+        self.gather = None
 
     def forward(self, x: Tensor, cos: Tensor, sin: Tensor) -> Tensor:
         B, S, _ = x.shape
-        q = self.wq(x).view(B, S, -1, self.head_dim)
-        k = self.wk(x).view(B, S, -1, self.head_dim)
-        v = self.wv(x).view(B, S, -1, self.head_dim)
+        if self.gather is not None:
+            q, k, v = (t.view(B, S, -1, self.head_dim) for t in self.gather(x))
+        else:
+            q = self.wq(x).view(B, S, -1, self.head_dim)
+            k = self.wk(x).view(B, S, -1, self.head_dim)
+            v = self.wv(x).view(B, S, -1, self.head_dim)
         q, k = apply_rope(q, cos, sin), apply_rope(k, cos, sin)
         q, k, v = (t.transpose(1, 2) for t in (q, k, v))
         o = F.scaled_dot_product_attention(q, k, v, is_causal=True, enable_gqa=self.n_kv_heads != self.n_heads)
@@ -103,8 +109,12 @@ class FeedForward(nn.Module):
         self.w1 = nn.Linear(dim, hidden, bias=False)  # gate
         self.w3 = nn.Linear(dim, hidden, bias=False)  # up
         self.w2 = nn.Linear(hidden, dim, bias=False)  # down
+        self.gather = None  # gate/up through the fused all-gather + GEMM (see Attention)
 
     def forward(self, x: Tensor) -> Tensor:
+        if self.gather is not None:
+            gate, up = self.gather(x)
+            return self.w2(_model_ops.swiglu(gate, up))
         return self.w2(_model_ops.swiglu(self.w1(x), self.w3(x)))
 
 

@@ -1,25 +1,30 @@
 // Parameter all-gather fused into the forward GEMM (FSDP "all-gather -> first
 // forward GEMM" as one kernel).
 //
-//   out[M, N] = x[M, K] @ W[N, K]^T,   W row-sharded over `world` ranks:
-//   rank r holds rows [r * N/W, (r + 1) * N/W) (FSDP dim-0 shard).
+//   out_s[M, N_s] = x[M, K] @ W_s[N_s, K]^T  for up to 4 weights W_s (e.g. the
+//   q, k, v projections, or gate and up) that share the input x. Each W_s is
+//   row-sharded over `world` ranks: rank r holds rows [r * N_s/W, (r+1) * N_s/W)
+//   (FSDP dim-0 shard). The gathered weights land in one local buffer
+//   wg[sum N_s, K] (W_s at rows [row0_s, row0_s + N_s)), kept for the backward.
 //
 // One persistent cta_group::2 kernel does both the gather and the GEMM:
 //   * warps 10..13 of every CTA are gather warps. They take 4 KiB pieces of W
 //     from one work counter in a fixed order: first this rank's own chunks
 //     (its shard -> its symmetric slot for the peers, and -> the local gathered
 //     copy `wg`), then the peers' chunks (P2P 16-byte loads from the peer's
-//     slot over NVLink -> `wg`). Chunk = 256 rows of W = one N tile. Every
+//     slot over NVLink -> `wg`). Chunk = 128 rows of wg = one CTA's half of a
+//     256-row N tile; the order (own rank first, then rank + 1, ...) comes
+//     from a host-built table. Every
 //     finished piece bumps its chunk's done counter (release). When the last
 //     local piece lands, the rank announces "slot ready for this epoch" to
 //     every peer (release store at system scope into the peers' flag arrays).
 //     A gather warp reads a peer's slot only after that peer's flag reached
 //     this epoch (acquire, bounded wait).
-//   * warp 0 (TMA producer) walks output tiles chunk by chunk in the same
-//     rotated order (own chunks first, then rank+1's, ...), so the MMA starts on
+//   * warp 0 (TMA producer) walks output tiles in an order that follows the
+//     gather order (tiles whose chunks are all local first), so the MMA starts on
 //     local data immediately and each remote chunk is needed only after the
 //     gather warps had time to bring it. Before the first TMA load of a B tile
-//     it waits (bounded) until that chunk's done counter is complete, then
+//     it waits (bounded) until its CTA's chunk counter is complete, then
 //     issues a proxy fence so the async proxy sees the generic-proxy stores.
 //     TMA only ever reads this GPU's own memory (x and wg); nothing is a
 //     cluster-multicast load.
@@ -69,20 +74,31 @@ constexpr int TMEM_COLS = 512;
 constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 + 256;
 constexpr int PIECE_U = 8;                         // 16-byte loads in flight per lane
 constexpr int PIECE_BYTES = 32 * 16 * PIECE_U;     // 4 KiB per warp-piece
-constexpr int MAX_CHUNKS = 1024;                   // N <= 262144
+constexpr int CHUNK_ROWS = 128;
+constexpr int MAX_SEGS = 4;
+constexpr int MAX_CHUNKS = 2048;                   // sum N_s <= 262144
 constexpr int CTR_STRIDE = 2 + MAX_CHUNKS;         // [ticket, local_done, done[chunk]...]
+
+struct Seg {
+  const uint8_t* shard;  // this rank's rows of W_s (local memory)
+  __nv_bfloat16* out;    // [M, rows]
+  int row0, rows, rpr;   // first row in wg, total rows, rows per rank
+  long long slot_off;    // byte offset of W_s's shard inside every rank's slot
+};
 
 struct AgArgs {
   int tiles_m, tiles_n, num_kb;
-  int rank, world, cpr;  // cpr: chunks per rank
-  long long chunk_bytes;
-  int ppc;               // pieces per chunk
-  __nv_bfloat16* out;
-  int ldo;
+  int rank, world, nseg;
+  Seg seg[MAX_SEGS];
+  long long row_bytes;       // K * 2
+  long long chunk_bytes;     // CHUNK_ROWS * row_bytes
+  int ppc;                   // pieces per chunk
+  int local_chunks;          // the first local_chunks entries of gather_order are this rank's
+  const int* gather_order;   // [tiles_n * 2] chunk ids in gather order
+  const int* tile_order;     // [tiles_n] N tiles in processing order
   uint8_t* wg;
-  const uint8_t* shard;
   const int64_t* peer_base;  // [world] symmetric data buffers (world > 1)
-  long long slot_off;
+  long long slot_base;       // this call's slot (parity) in every rank's buffer
   const int64_t* flag_base;  // [world] flag arrays (uint32 per source rank)
   unsigned epoch;
   int* ctr;                  // this call's parity block
@@ -104,15 +120,17 @@ __device__ __forceinline__ void fence_proxy_async_global() {
   asm volatile("fence.proxy.async.global;" ::: "memory");
 }
 
-// Rotated chunk order: j -> actual chunk (N tile) index; j < cpr are this rank's.
-__device__ __forceinline__ int chunk_of(const AgArgs& p, int j) {
-  int c = j + p.rank * p.cpr;
-  return c >= p.tiles_n ? c - p.tiles_n : c;
+__device__ __forceinline__ int seg_of_row(const AgArgs& p, int row) {
+  int s = 0;
+#pragma unroll
+  for (int i = 1; i < MAX_SEGS; ++i)
+    if (i < p.nseg && row >= p.seg[i].row0) s = i;
+  return s;
 }
 
 __device__ void gather_role(const AgArgs& p, int lane, volatile int* abort_flag) {
-  const int total = p.tiles_n * p.ppc;
-  const int local_total = p.cpr * p.ppc;
+  const int total = 2 * p.tiles_n * p.ppc;
+  const int local_total = p.local_chunks * p.ppc;
   unsigned long long ready_mask = 0;  // peers seen ready (world <= 64)
   while (true) {
     int t = 0;
@@ -121,21 +139,24 @@ __device__ void gather_role(const AgArgs& p, int lane, volatile int* abort_flag)
     if (t >= total || *abort_flag) break;
     const int j = t / p.ppc;
     const int piece = t - j * p.ppc;
-    const int chunk = chunk_of(p, j);
+    const int chunk = p.gather_order[j];
+    const int row = chunk * CHUNK_ROWS;
+    const Seg& sg = p.seg[seg_of_row(p, row)];
+    const int rr = row - sg.row0;
+    const int src_rank = rr / sg.rpr;
+    const long long src_off = (long long)(rr - src_rank * sg.rpr) * p.row_bytes;  // inside the rank's shard
     const long long in_chunk = (long long)piece * PIECE_BYTES + lane * 16;
     uint4 v[PIECE_U];
     if (t < local_total) {
-      const uint8_t* src = p.shard + (long long)j * p.chunk_bytes + in_chunk;
+      const uint8_t* src = sg.shard + src_off + in_chunk;
 #pragma unroll
       for (int u = 0; u < PIECE_U; ++u) v[u] = *reinterpret_cast<const uint4*>(src + u * 512);
       if (p.world > 1) {
-        uint8_t* slot = reinterpret_cast<uint8_t*>(p.peer_base[p.rank]) + p.slot_off + (long long)j * p.chunk_bytes +
-                        in_chunk;
+        uint8_t* slot = reinterpret_cast<uint8_t*>(p.peer_base[p.rank]) + p.slot_base + sg.slot_off + src_off + in_chunk;
 #pragma unroll
         for (int u = 0; u < PIECE_U; ++u) *reinterpret_cast<uint4*>(slot + u * 512) = v[u];
       }
     } else {
-      const int src_rank = chunk / p.cpr;
       if (!(ready_mask & (1ull << src_rank))) {
         bool ok = true;
         if (lane == 0) {
@@ -160,8 +181,8 @@ __device__ void gather_role(const AgArgs& p, int lane, volatile int* abort_flag)
         __threadfence_system();
         ready_mask |= 1ull << src_rank;
       }
-      const uint8_t* src = reinterpret_cast<const uint8_t*>(p.peer_base[src_rank]) + p.slot_off +
-                           (long long)(chunk - src_rank * p.cpr) * p.chunk_bytes + in_chunk;
+      const uint8_t* src = reinterpret_cast<const uint8_t*>(p.peer_base[src_rank]) + p.slot_base + sg.slot_off +
+                           src_off + in_chunk;
 #pragma unroll
       for (int u = 0; u < PIECE_U; ++u) v[u] = *reinterpret_cast<const uint4*>(src + u * 512);
     }
@@ -189,7 +210,8 @@ __device__ void gather_role(const AgArgs& p, int lane, volatile int* abort_flag)
 }
 
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
-    ag_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, const AgArgs p) {
+    ag_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                   const __grid_constant__ AgArgs p) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sA = smem;
@@ -243,10 +265,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
     for (int t = cid; ok && t < total_tiles; t += ncl) {
       const int j = t / p.tiles_m;
       const int tm = t - j * p.tiles_m;
-      const int tn = chunk_of(p, j);
+      const int tn = p.tile_order[j];
       if (tn != ready_chunk) {
         if (lane == 0) {
-          const int* c = p.ctr + 2 + tn;
+          const int* c = p.ctr + 2 + 2 * tn + (int)crank;  // this CTA loads rows [128 crank, +128) of the tile
           const unsigned long long t0 = global_timer_ns();
           while (ld_acquire_gpu(c) < p.ppc) {
             if (*abort_flag) {
@@ -341,7 +363,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
     for (int t = cid; t < total_tiles; t += ncl) {
       const int j = t / p.tiles_m;
       const int tm = t - j * p.tiles_m;
-      const int tn = chunk_of(p, j);
+      const int tn = p.tile_order[j];
+      const Seg& sg = p.seg[seg_of_row(p, tn * TN)];
       if (!mbar_wait(&tfull[acc], acc_phase, abort_flag, p.err)) break;
       tc_fence_after();
       const int row = tm * TM + (int)crank * 128 + q * 32 + lane;
@@ -349,8 +372,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
       for (int c = half * (TN / 64); c < (half + 1) * (TN / 64); ++c) {
         uint32_t r[32];
         tmem_ld_32cols(tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc * TN + c * 32), r);
-        const int col0 = tn * TN + c * 32;
-        uint4* op = reinterpret_cast<uint4*>(p.out + (long long)row * p.ldo + col0);
+        const int col0 = tn * TN - sg.row0 + c * 32;
+        uint4* op = reinterpret_cast<uint4*>(sg.out + (long long)row * sg.rows + col0);
 #pragma unroll
         for (int u = 0; u < 4; ++u) {
           uint4 x;
@@ -393,36 +416,33 @@ int sm_count_ag(int dev) {
 
 }  // namespace
 
-// out[M, N] = x[M, K] @ W^T with W gathered from every rank's shard into wg[N, K]
-// (see the top of this file). x, shard, wg, out: contiguous bf16 CUDA tensors.
-// peer_base / flag_base: int64 [world] device tensors (ignored when world == 1).
-// counters: int32 [2 * (2 + 1024)] device tensor, zero before the first call of a
-// sequence, owned by one stream. max_pairs > 0 caps the number of CTA pairs.
-void ag_gemm(const at::Tensor& x, const at::Tensor& shard, at::Tensor& wg, at::Tensor& out,
-             const at::Tensor& peer_base, int64_t slot_off, const at::Tensor& flag_base, at::Tensor& counters,
-             int64_t rank, int64_t world, int64_t epoch, int64_t max_pairs) {
+// out_s = x @ W_s^T for every segment s, with each W_s gathered from every
+// rank's shard into rows [row0_s, row0_s + N_s) of wg (see the top of this file).
+// x [M, K], shards[s] [N_s / world, K], wg [sum N_s, K], outs[s] [M, N_s]:
+// contiguous bf16 CUDA tensors. order: int32 [2 * tiles_n + tiles_n] device
+// table (gather order of the 128-row chunks, own rank's first, then the N-tile
+// processing order); local_chunks: how many leading gather entries are local.
+// slot_offs[s]: byte offset of shard s inside a rank's slot. peer_base /
+// flag_base: int64 [world] device tensors (ignored when world == 1). counters:
+// int32 [2 * (2 + 2048)], zero before the first call, owned by one stream.
+void ag_gemm(const at::Tensor& x, const std::vector<at::Tensor>& shards, at::Tensor& wg,
+             const std::vector<at::Tensor>& outs, const at::Tensor& order, int64_t local_chunks,
+             const std::vector<int64_t>& slot_offs, const at::Tensor& peer_base, int64_t slot_base,
+             const at::Tensor& flag_base, at::Tensor& counters, int64_t rank, int64_t world, int64_t epoch,
+             int64_t max_pairs) {
   auto bf16_2d = [](const at::Tensor& t, const char* name) {
     TORCH_CHECK(t.is_cuda() && t.dim() == 2 && t.scalar_type() == at::kBFloat16 && t.is_contiguous(), name,
                 ": contiguous 2-D bf16 CUDA tensor expected");
   };
   bf16_2d(x, "x");
-  bf16_2d(shard, "shard");
   bf16_2d(wg, "wg");
-  bf16_2d(out, "out");
   const int64_t M = x.size(0), K = x.size(1), N = wg.size(0);
+  const int nseg = (int)shards.size();
+  TORCH_CHECK(nseg >= 1 && nseg <= MAX_SEGS && (int)outs.size() == nseg && (int)slot_offs.size() == nseg,
+              "1..4 segments with one output and slot offset each");
   TORCH_CHECK(world >= 1 && world <= 64 && rank >= 0 && rank < world, "bad rank/world");
-  TORCH_CHECK(wg.size(1) == K && shard.size(1) == K && shard.size(0) * world == N, "shard [N/world, K], wg [N, K]");
-  TORCH_CHECK(out.size(0) == M && out.size(1) == N, "out must be [M, N]");
-  TORCH_CHECK(M % 256 == 0 && K % 64 == 0 && shard.size(0) % 256 == 0,
-              "M and rows per rank must be multiples of 256, K a multiple of 64");
-  TORCH_CHECK(N / 256 <= MAX_CHUNKS, "N too large");
-  TORCH_CHECK(counters.is_cuda() && counters.scalar_type() == at::kInt && counters.numel() >= 2 * CTR_STRIDE,
-              "counters: int32 [2 * (2 + 1024)]");
-  if (world > 1) {
-    TORCH_CHECK(peer_base.is_cuda() && peer_base.scalar_type() == at::kLong && peer_base.numel() == world);
-    TORCH_CHECK(flag_base.is_cuda() && flag_base.scalar_type() == at::kLong && flag_base.numel() == world);
-    TORCH_CHECK(slot_off % 16 == 0, "slot offset must be 16-byte aligned");
-  }
+  TORCH_CHECK(M % 256 == 0 && K % 64 == 0 && wg.size(1) == K, "M must be a multiple of 256, K of 64");
+  TORCH_CHECK(N % 256 == 0 && N / CHUNK_ROWS <= MAX_CHUNKS, "sum of rows must be a multiple of 256, at most 262144");
   const at::cuda::CUDAGuard guard(x.device());
   const int dev = x.get_device();
   AgArgs p{};
@@ -431,15 +451,44 @@ void ag_gemm(const at::Tensor& x, const at::Tensor& shard, at::Tensor& wg, at::T
   p.num_kb = (int)(K / BK);
   p.rank = (int)rank;
   p.world = (int)world;
-  p.cpr = (int)(shard.size(0) / 256);
-  p.chunk_bytes = 256LL * K * 2;
+  p.nseg = nseg;
+  int row0 = 0;
+  for (int i = 0; i < nseg; ++i) {
+    bf16_2d(shards[i], "shard");
+    bf16_2d(outs[i], "out");
+    const int64_t rows = shards[i].size(0) * world;
+    TORCH_CHECK(shards[i].size(1) == K && shards[i].size(0) % CHUNK_ROWS == 0 && rows % 256 == 0,
+                "shard s: [N_s / world, K] with N_s / world a multiple of 128 and N_s a multiple of 256");
+    TORCH_CHECK(outs[i].size(0) == M && outs[i].size(1) == rows, "out s must be [M, N_s]");
+    TORCH_CHECK(slot_offs[i] % 16 == 0, "slot offsets must be 16-byte aligned");
+    p.seg[i].shard = reinterpret_cast<const uint8_t*>(shards[i].data_ptr());
+    p.seg[i].out = reinterpret_cast<__nv_bfloat16*>(outs[i].data_ptr());
+    p.seg[i].row0 = row0;
+    p.seg[i].rows = (int)rows;
+    p.seg[i].rpr = (int)shards[i].size(0);
+    p.seg[i].slot_off = slot_offs[i];
+    row0 += (int)rows;
+  }
+  TORCH_CHECK(row0 == N, "wg must have sum N_s rows");
+  TORCH_CHECK(order.is_cuda() && order.scalar_type() == at::kInt && order.numel() == 3 * p.tiles_n,
+              "order: int32 [3 * N / 256]");
+  TORCH_CHECK(local_chunks >= 0 && local_chunks <= 2 * p.tiles_n);
+  TORCH_CHECK(counters.is_cuda() && counters.scalar_type() == at::kInt && counters.numel() >= 2 * CTR_STRIDE,
+              "counters: int32 [2 * (2 + 2048)]");
+  if (world > 1) {
+    TORCH_CHECK(peer_base.is_cuda() && peer_base.scalar_type() == at::kLong && peer_base.numel() == world);
+    TORCH_CHECK(flag_base.is_cuda() && flag_base.scalar_type() == at::kLong && flag_base.numel() == world);
+    TORCH_CHECK(slot_base % 16 == 0, "slot base must be 16-byte aligned");
+  }
+  p.row_bytes = K * 2;
+  p.chunk_bytes = CHUNK_ROWS * p.row_bytes;
   p.ppc = (int)(p.chunk_bytes / PIECE_BYTES);
-  p.out = reinterpret_cast<__nv_bfloat16*>(out.data_ptr());
-  p.ldo = (int)N;
+  p.local_chunks = (int)local_chunks;
+  p.gather_order = order.data_ptr<int>();
+  p.tile_order = order.data_ptr<int>() + 2 * p.tiles_n;
   p.wg = reinterpret_cast<uint8_t*>(wg.data_ptr());
-  p.shard = reinterpret_cast<const uint8_t*>(shard.data_ptr());
   p.peer_base = world > 1 ? peer_base.data_ptr<int64_t>() : nullptr;
-  p.slot_off = slot_off;
+  p.slot_base = slot_base;
   p.flag_base = world > 1 ? flag_base.data_ptr<int64_t>() : nullptr;
   p.epoch = (unsigned)epoch;
   int* ctr = counters.data_ptr<int>();

@@ -63,9 +63,11 @@ void push_slots(const at::Tensor& src, const at::Tensor& peer_base, int64_t off,
                 int64_t world, bool per_peer, int64_t max_ctas);
 void pull_slots(at::Tensor& out, const at::Tensor& peer_base, int64_t off, int64_t slot_bytes, int64_t rank,
                 int64_t world, int64_t max_ctas);
-void ag_gemm(const at::Tensor& x, const at::Tensor& shard, at::Tensor& wg, at::Tensor& out,
-             const at::Tensor& peer_base, int64_t slot_off, const at::Tensor& flag_base, at::Tensor& counters,
-             int64_t rank, int64_t world, int64_t epoch, int64_t max_pairs);
+void ag_gemm(const at::Tensor& x, const std::vector<at::Tensor>& shards, at::Tensor& wg,
+             const std::vector<at::Tensor>& outs, const at::Tensor& order, int64_t local_chunks,
+             const std::vector<int64_t>& slot_offs, const at::Tensor& peer_base, int64_t slot_base,
+             const at::Tensor& flag_base, at::Tensor& counters, int64_t rank, int64_t world, int64_t epoch,
+             int64_t max_pairs);
 void allreduce_inplace(const at::Tensor& peer_base, int64_t off, int64_t nbytes, int64_t dtype_code, int64_t rank,
                        int64_t world, int64_t mc_base, int64_t max_ctas);
 void flag_signal(const at::Tensor& flag_base, int64_t slot, int64_t rank, int64_t world, int64_t epoch);

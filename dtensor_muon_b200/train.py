@@ -28,6 +28,7 @@ def build_llama(
     block_factory=None,
     reshard_after_forward: bool = False,
     fsdp_comm: str = "p2p",
+    fused_gather: bool = False,
 ) -> Llama:
     """Build a randomly initialised Llama on ``device`` without a host copy.
 
@@ -39,15 +40,31 @@ def build_llama(
     ``fsdp_comm="p2p"`` runs FSDP's all-gather / reduce-scatter on the NVLink
     peer-memory kernels of :mod:`dtensor_muon_b200.parallel.fsdp_comm`;
     ``"nccl"`` keeps FSDP2's NCCL collectives.
+    ``fused_gather=True`` (with ``mesh``) takes the q/k/v and gate/up weights out
+    of FSDP: they become ``Shard(0)`` DTensors applied by the fused parameter
+    all-gather + GEMM kernel (:class:`dtensor_muon_b200.parallel.ag_gemm.GatherLinear`),
+    whose gather runs inside the GEMM instead of ahead of it.
     """
     with torch.device("meta"):
         model = Llama(cfg, block_factory=block_factory).to(dtype)
     if mesh is not None:
         from torch.distributed.fsdp import fully_shard
 
+        ignored: set = set()
+        if fused_gather:
+            from .parallel.ag_gemm import GatherLinear
+
+            for layer in model.layers:
+                att, ffn = layer.attention, layer.feed_forward
+                att.gather = GatherLinear([att.wq, att.wk, att.wv], mesh)
+                ignored.update(att.gather.params)
+                if hasattr(ffn, "w1") and hasattr(ffn, "w3"):
+                    ffn.gather = GatherLinear([ffn.w1, ffn.w3], mesh)
+                    ignored.update(ffn.gather.params)
+        kw = dict(ignored_params=ignored) if ignored else {}
         for layer in model.layers:
-            fully_shard(layer, mesh=mesh, reshard_after_forward=reshard_after_forward)
-        fully_shard(model, mesh=mesh, reshard_after_forward=reshard_after_forward)
+            fully_shard(layer, mesh=mesh, reshard_after_forward=reshard_after_forward, **kw)
+        fully_shard(model, mesh=mesh, reshard_after_forward=reshard_after_forward, **kw)
         # Issue each block's parameter all-gather two blocks ahead of its forward.
         layers = list(model.layers)
         for i, layer in enumerate(layers):
