@@ -255,8 +255,9 @@ def parse_args():
                     help="ours, N > 1: Muon momentum update inside the FSDP gradient reduce-scatter")
     ap.add_argument("--fsdp-comm", default=os.environ.get("DMB_FSDP_COMM", "p2p"), choices=["p2p", "nccl"],
                     help="ours: FSDP collectives on NVLink P2P kernels or NCCL")
-    ap.add_argument("--fused-gather", type=int, default=int(os.environ.get("DMB_FUSED_GATHER", "0")),
-                    help="ours, N > 1: q/k/v and gate/up weights gathered inside their forward GEMM")
+    ap.add_argument("--fused-gather", type=int, default=int(os.environ.get("DMB_FUSED_GATHER", "1")),
+                    help="ours, N > 1: q/k/v and gate/up weights gathered inside their forward GEMM "
+                         "(0: every weight through FSDP2's all-gather)")
     ap.add_argument("--ref-batch-size", type=int, default=32,
                     help="reference arm: Muon foreach batch_size (keeps its Gram kernel below 2**31 elements)")
     args = ap.parse_args()
