@@ -144,7 +144,7 @@ def build_ours(args, world, device):
 
         mesh = init_device_mesh("cuda", (world,))
     model = build_llama(cfg, device, mesh=mesh, seed=0, fsdp_comm=args.fsdp_comm,
-                        fused_gather=world > 1 and bool(args.fused_gather))
+                        fused_gather={0: False, 1: True, 2: "all"}[args.fused_gather] if world > 1 else False)
     opt = build_optimizer(model, Muon, lr=args.lr, wd=0.1, orthogonalization_strategy=args.strategy,
                           fuse_momentum=world > 1 and args.fsdp_comm == "p2p" and args.fuse_momentum)
     from dtensor_muon_b200.models.llama import lm_loss
@@ -257,7 +257,7 @@ def parse_args():
                     help="ours: FSDP collectives on NVLink P2P kernels or NCCL")
     ap.add_argument("--fused-gather", type=int, default=int(os.environ.get("DMB_FUSED_GATHER", "1")),
                     help="ours, N > 1: q/k/v and gate/up weights gathered inside their forward GEMM "
-                         "(0: every weight through FSDP2's all-gather)")
+                         "(0: every weight through FSDP2's all-gather; 2: wo and w2 too)")
     ap.add_argument("--ref-batch-size", type=int, default=32,
                     help="reference arm: Muon foreach batch_size (keeps its Gram kernel below 2**31 elements)")
     args = ap.parse_args()

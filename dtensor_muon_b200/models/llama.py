@@ -88,6 +88,7 @@ class Attention(nn.Module):
         # set by train.build_llama(fused_gather=True): q/k/v through the fused
         # parameter all-gather + GEMM kernel (parallel.ag_gemm.GatherLinear)
         self.gather = None
+        self.gather_out = None  # wo through the fused gather (one-weight GatherLinear)
 
     def forward(self, x: Tensor, cos: Tensor, sin: Tensor) -> Tensor:
         B, S, _ = x.shape
@@ -100,7 +101,10 @@ class Attention(nn.Module):
         q, k = apply_rope(q, cos, sin), apply_rope(k, cos, sin)
         q, k, v = (t.transpose(1, 2) for t in (q, k, v))
         o = F.scaled_dot_product_attention(q, k, v, is_causal=True, enable_gqa=self.n_kv_heads != self.n_heads)
-        return self.wo(o.transpose(1, 2).reshape(B, S, -1))
+        o = o.transpose(1, 2).reshape(B, S, -1)
+        if self.gather_out is not None:
+            return self.gather_out(o)[0]
+        return self.wo(o)
 
 
 class FeedForward(nn.Module):
@@ -110,11 +114,13 @@ class FeedForward(nn.Module):
         self.w3 = nn.Linear(dim, hidden, bias=False)  # up
         self.w2 = nn.Linear(hidden, dim, bias=False)  # down
         self.gather = None  # gate/up through the fused all-gather + GEMM (see Attention)
+        self.gather_out = None  # w2 likewise
 
     def forward(self, x: Tensor) -> Tensor:
         if self.gather is not None:
             gate, up = self.gather(x)
-            return self.w2(_model_ops.swiglu(gate, up))
+            h = _model_ops.swiglu(gate, up)
+            return self.gather_out(h)[0] if self.gather_out is not None else self.w2(h)
         return self.w2(_model_ops.swiglu(self.w1(x), self.w3(x)))
 
 

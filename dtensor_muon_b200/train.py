@@ -28,7 +28,7 @@ def build_llama(
     block_factory=None,
     reshard_after_forward: bool = False,
     fsdp_comm: str = "p2p",
-    fused_gather: bool = False,
+    fused_gather: bool | str = False,
 ) -> Llama:
     """Build a randomly initialised Llama on ``device`` without a host copy.
 
@@ -43,7 +43,8 @@ def build_llama(
     ``fused_gather=True`` (with ``mesh``) takes the q/k/v and gate/up weights out
     of FSDP: they become ``Shard(0)`` DTensors applied by the fused parameter
     all-gather + GEMM kernel (:class:`dtensor_muon_b200.parallel.ag_gemm.GatherLinear`),
-    whose gather runs inside the GEMM instead of ahead of it.
+    whose gather runs inside the GEMM instead of ahead of it; ``fused_gather="all"``
+    does the same for wo and w2 (only the norms stay in FSDP2).
     """
     with torch.device("meta"):
         model = Llama(cfg, block_factory=block_factory).to(dtype)
@@ -58,9 +59,15 @@ def build_llama(
                 att, ffn = layer.attention, layer.feed_forward
                 att.gather = GatherLinear([att.wq, att.wk, att.wv], mesh)
                 ignored.update(att.gather.params)
+                if fused_gather == "all":
+                    att.gather_out = GatherLinear([att.wo], mesh)
+                    ignored.update(att.gather_out.params)
                 if hasattr(ffn, "w1") and hasattr(ffn, "w3"):
                     ffn.gather = GatherLinear([ffn.w1, ffn.w3], mesh)
                     ignored.update(ffn.gather.params)
+                    if fused_gather == "all":
+                        ffn.gather_out = GatherLinear([ffn.w2], mesh)
+                        ignored.update(ffn.gather_out.params)
         kw = dict(ignored_params=ignored) if ignored else {}
         for layer in model.layers:
             fully_shard(layer, mesh=mesh, reshard_after_forward=reshard_after_forward, **kw)

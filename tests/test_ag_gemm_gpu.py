@@ -133,7 +133,7 @@ def _train_worker(rank, world):
     mesh = init_device_mesh("cuda", (world,))
     cfg = preset("tiny", dim=512, n_heads=4, n_kv_heads=2, ffn_dim=1024)
     losses, finals = {}, {}
-    for fused in (False, True):
+    for fused in (False, True, "all"):
         model = build_llama(cfg, dev, mesh=mesh, seed=0, fsdp_comm="nccl", fused_gather=fused)
         # identical weights in both runs: a seeded full tensor per parameter
         gen = torch.Generator().manual_seed(11)
@@ -154,10 +154,11 @@ def _train_worker(rank, world):
         _ext.check_device_errors(dev)
         losses[fused] = ls
         finals[fused] = {n: p.full_tensor().float() for n, p in model.named_parameters()}
-    for a, b in zip(losses[False], losses[True]):
-        assert abs(a - b) < 2e-2 * max(1.0, abs(a)), (losses[False], losses[True])
-    for n, p in finals[False].items():
-        assert_close(finals[True][n], p, rtol=5e-2, atol=5e-3, max_mismatch_pct=2.0, msg=n)
+    for mode in (True, "all"):
+        for a, b in zip(losses[False], losses[mode]):
+            assert abs(a - b) < 2e-2 * max(1.0, abs(a)), (mode, losses[False], losses[mode])
+        for n, p in finals[False].items():
+            assert_close(finals[mode][n], p, rtol=5e-2, atol=5e-3, max_mismatch_pct=2.0, msg=f"{mode} {n}")
     dist.barrier()
 
 

@@ -28,6 +28,10 @@ def _worker(rank, world):
             assert w.to_local().device.type == "cpu" and torch.isfinite(w.to_local()).all()
         for p in att.gather.params + ffn.gather.params:
             assert p.requires_grad
+    model2 = build_llama(cfg, torch.device("cpu"), mesh=mesh, seed=0, fsdp_comm="nccl", fused_gather="all")
+    for layer in model2.layers:
+        assert layer.attention.gather_out is not None and layer.feed_forward.gather_out is not None
+        assert isinstance(layer.attention.wo.weight, DTensor) and tuple(layer.feed_forward.w2.weight.shape) == (512, 1024)
     muon, adam = muon_and_adam_params(model)
     assert len(muon) == 2 * 7 and all(isinstance(p, DTensor) for p in muon + adam)
 
