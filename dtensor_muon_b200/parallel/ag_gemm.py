@@ -160,6 +160,30 @@ class _GatherLinearFn(torch.autograd.Function):
         return (dx.view(*ctx.lead, wg.shape[1]), None) + (None,) * len(dys)
 
 
+_RS: dict = {}
+
+
+def _reduce_scatter(group):
+    """Reduce-scatter used for the weight gradients: the copy-engine scatter + fp32
+    local sum over peer memory (``fsdp_comm.P2PReduceScatter``, its own workspace
+    because it runs on the side stream), or NCCL when symmetric memory is
+    unavailable or ``DMB_GATHER_RS=nccl``."""
+    import os
+
+    key = group.group_name
+    rs = _RS.get(key)
+    if rs is None:
+        if os.environ.get("DMB_GATHER_RS", "p2p") == "p2p" and symm.available():
+            from .fsdp_comm import P2PReduceScatter
+
+            rs = P2PReduceScatter(purpose="gather_linear_rs")
+        else:
+            def rs(out, inp, grp, op):
+                dist.reduce_scatter_tensor(out, inp, op=op, group=grp)
+        _RS[key] = rs
+    return rs
+
+
 class GatherLinear:
     """Up to four ``nn.Linear`` layers that read the same input (q/k/v, gate/up),
     their weights kept as ``Shard(0)`` DTensors over a 1-D mesh (FSDP layout, so
@@ -228,7 +252,7 @@ class GatherLinear:
                         torch.matmul(dy[:, r * n:(r + 1) * n].t(), x2, out=packed[r, off:off + n])
                         off += n
                 red = torch.empty(tot, x2.shape[1], dtype=x2.dtype, device=x2.device)
-                dist.reduce_scatter_tensor(red, packed.view(world * tot, -1), op=dist.ReduceOp.AVG, group=self.group)
+                _reduce_scatter(self.group)(red, packed.view(world * tot, -1), self.group, dist.ReduceOp.AVG)
                 grads, off = [], 0
                 for n in rpr:
                     grads.append(red[off:off + n])

@@ -139,8 +139,10 @@ class P2PReduceScatter(ReduceScatter):
     Muon parameters (``rs_sum_momentum``) and leaves g' as their gradient.
     """
 
-    def __init__(self, module=None, fused=None):
-        self._stage = _staging("fsdp_rs")
+    def __init__(self, module=None, fused=None, purpose: str = "fsdp_rs"):
+        # callers that issue reduce-scatters on another stream pass their own purpose
+        # (own symmetric workspace, own barrier sequence)
+        self._stage = _staging(purpose)
         self._module = module
         self._fused = fused
 
