@@ -257,9 +257,10 @@ class GatherLinear:
                 for n in rpr:
                     grads.append(red[off:off + n])
                     off += n
-        if not GatherLinear._pending:
-            torch.autograd.Variable._execution_engine.queue_callback(GatherLinear._finish)
         GatherLinear._pending.append((self, grads, side))
+        # one callback per call: the first to run delivers every pending gradient, the
+        # rest find the list empty (a backward that raised leaves nothing queued behind)
+        torch.autograd.Variable._execution_engine.queue_callback(GatherLinear._finish)
 
     @staticmethod
     def _finish():
@@ -267,8 +268,10 @@ class GatherLinear:
 
         pending, GatherLinear._pending = GatherLinear._pending, []
         for owner, grads, side in pending:
-            torch.cuda.current_stream(grads[0].device).wait_stream(side)
+            cur = torch.cuda.current_stream(grads[0].device)
+            cur.wait_stream(side)
             for p, g in zip(owner.params, grads):
+                g.record_stream(cur)  # allocated on the side stream, consumed on this one
                 if isinstance(p, DTensor):
                     g = DTensor.from_local(g, owner.mesh, [Shard(0)], run_check=False, shape=p.shape,
                                            stride=p.stride())
