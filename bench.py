@@ -31,7 +31,7 @@ import torch
 import torch.distributed as dist
 
 HERE = os.path.dirname(os.path.abspath(__file__))
-BASELINE_VALUE = None  # the reference publishes no B200 tokens/s (BASELINE.json "published": {})
+BASELINE_VALUE = None  # the reference publishes no B200 tokens/s for this config
 METRIC = "Muon optimizer.step() ms and train tokens/s, Llama-8B FSDP at 1/2/4/8 B200"
 
 

@@ -2,7 +2,7 @@
 
     python -m torch.distributed.run --nproc-per-node W benchmarks/bench_distributed.py [--impl ours|reference]
 
-Shapes: 4096x4096, 4096x14336, 14336x4096 (one matrix each,
+Shapes (orthogonalisation microbench): 4096x4096, 4096x14336, 14336x4096 (one matrix each,
 its rows sharded over the W ranks: a 2-D ``Shard(0)`` DTensor) and 64 x 1024x1024
 (a 3-D ``Shard(0)`` stack: each rank holds 64/W whole matrices). Entries N(0,1),
 seed 0, Frobenius-normalised; Newton-Schulz and Polar Express, 5 steps.

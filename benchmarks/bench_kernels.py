@@ -2,7 +2,7 @@
 against cuBLAS-based PyTorch (and, with --with-reference, the reference's Triton
 Gram and compiled loops from baseline/_ref).
 
-Config-2 shapes (BASELINE): 4096x4096, 4096x14336, 14336x4096 and 64 x 1024x1024,
+Config-2 shapes (the headline orthogonalisation microbench): 4096x4096, 4096x14336, 14336x4096 and 64 x 1024x1024,
 bf16 inputs N(0,1), 5 steps. Reports ms and the fraction of the measured bf16
 peak for the dense FLOP count (the symmetric kernels do less actual work, so a
 fraction above the cuBLAS denominator is expected).
