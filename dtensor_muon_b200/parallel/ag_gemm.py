@@ -217,6 +217,17 @@ class GatherLinear:
                 lin.weight = torch.nn.Parameter(
                     DTensor.from_local(local, mesh, [Shard(0)], run_check=False, shape=(n, k), stride=(k, 1)))
 
+    @staticmethod
+    def eligible(linears, world: int) -> bool:
+        """The kernel's layout rules: every weight has a multiple of 256 rows and of
+        128 rows per rank, K a multiple of 64 shared by all, at most four weights."""
+        ks = {lin.weight.shape[1] for lin in linears}
+        return (
+            1 <= len(linears) <= 4 and len(ks) == 1 and ks.pop() % 64 == 0
+            and all(lin.weight.shape[0] % 256 == 0 and lin.weight.shape[0] % (world * CHUNK_ROWS) == 0
+                    for lin in linears)
+        )
+
     @property
     def params(self):
         return [lin.weight for lin in self.linears]

@@ -55,19 +55,25 @@ def build_llama(
         if fused_gather:
             from .parallel.ag_gemm import GatherLinear
 
+            world = mesh.size()
+
+            def make(linears):
+                # groups the kernel's layout rules exclude stay on FSDP2
+                if not GatherLinear.eligible(linears, world):
+                    return None
+                g = GatherLinear(linears, mesh)
+                ignored.update(g.params)
+                return g
+
             for layer in model.layers:
                 att, ffn = layer.attention, layer.feed_forward
-                att.gather = GatherLinear([att.wq, att.wk, att.wv], mesh)
-                ignored.update(att.gather.params)
+                att.gather = make([att.wq, att.wk, att.wv])
                 if fused_gather == "all":
-                    att.gather_out = GatherLinear([att.wo], mesh)
-                    ignored.update(att.gather_out.params)
+                    att.gather_out = make([att.wo])
                 if hasattr(ffn, "w1") and hasattr(ffn, "w3"):
-                    ffn.gather = GatherLinear([ffn.w1, ffn.w3], mesh)
-                    ignored.update(ffn.gather.params)
-                    if fused_gather == "all":
-                        ffn.gather_out = GatherLinear([ffn.w2], mesh)
-                        ignored.update(ffn.gather_out.params)
+                    ffn.gather = make([ffn.w1, ffn.w3])
+                    if fused_gather == "all" and ffn.gather is not None:
+                        ffn.gather_out = make([ffn.w2])
         kw = dict(ignored_params=ignored) if ignored else {}
         for layer in model.layers:
             fully_shard(layer, mesh=mesh, reshard_after_forward=reshard_after_forward, **kw)

@@ -38,3 +38,18 @@ def _worker(rank, world):
 
 def test_fused_gather_model_layout():
     run_distributed(_worker, 2, backend="gloo", device_type="cpu", timeout_s=120)
+
+
+def test_eligibility_rules():
+    import torch
+
+    from dtensor_muon_b200.parallel.ag_gemm import GatherLinear
+
+    def lins(*shapes):
+        return [torch.nn.Linear(k, n, bias=False, device="meta") for n, k in shapes]
+
+    assert GatherLinear.eligible(lins((4096, 4096), (1024, 4096), (1024, 4096)), 8)
+    assert not GatherLinear.eligible(lins((4096, 4096), (1024, 4096), (1024, 4096)), 16)  # 64 k rows per rank
+    assert not GatherLinear.eligible(lins((512, 256), (512, 128)), 2)  # different K
+    assert not GatherLinear.eligible(lins((384, 256)), 1)  # rows not a multiple of 256
+    assert not GatherLinear.eligible(lins(*[(256, 256)] * 5), 1)  # more than four weights
