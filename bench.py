@@ -395,6 +395,10 @@ def run(args):
                 "parallelism": par,
                 "optimizer": f"Muon({args.strategy}, ns_steps=5) + AdamW(embed/norms/head)",
                 "l2": "no flush: every step streams >16 GB of weights/grads/state (inputs far larger than L2)",
+                **({"collectives": ("q/k/v + gate/up: all-gather fused into the forward GEMM"
+                                    + (" (+ wo, w2)" if args.fused_gather == 2 else "")
+                                    if args.fused_gather else "FSDP2 all-gather") + f"; FSDP2 comm {args.fsdp_comm}"}
+                   if world > 1 and args.impl == "ours" else {}),
             },
             clocks=clocks,
             e2e=e2e,
